@@ -1,0 +1,87 @@
+"""ctypes binding of libqkv.so (the C ABI declared in include/qkv.h).
+
+The shared library is the only compute path: if it is missing this module raises, it never
+substitutes anything else.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqkv.so")
+
+QKV_OK = 0
+QKV_EINVAL = -1
+QKV_EUNSUPPORTED = -2
+QKV_ECUDA = -3
+QKV_EWORKSPACE = -4
+QKV_EALIGN = -5
+QKV_EDEVICE = -6
+
+QKV_BF16, QKV_F16, QKV_F32 = 0, 1, 2
+QKV_MASK_NONE, QKV_MASK_CAUSAL, QKV_MASK_BOOL, QKV_MASK_ADDITIVE = 0, 1, 2, 3
+QKV_OUT_NORMALIZED, QKV_OUT_PARTIAL = 0, 1
+
+# every symbol include/qkv.h declares, with (restype, argtypes)
+_vp, _i, _ll, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_size_t
+SIGNATURES = {
+    "qkv_version": (_i, []),
+    "qkv_last_error": (ctypes.c_char_p, []),
+    "qkv_device_status": (_i, [_vp, _i]),
+    "qkv_quantize_append": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "qkv_dequantize": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
+    "qkv_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
+    "qkv_attention": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,  # q, kw, ks, kb, vw, vs, vb, out
+         _i, _i, _i, _i, _i, _i, _i,  # B HQ HKV S D NP n
+         _vp, _vp, _vp,  # lens pos_base total_lens
+         _i, _i, _i, _f,  # bits group_size dtype scale
+         _i, _vp, _i, _ll, _ll, _ll,  # mask_kind mask mask_nk strides
+         _i, _i, _vp, _sz, _vp],  # out_kind splits workspace ws_bytes stream
+    ),
+    "qkv_combine": (_i, [_vp, _i, _ll, _i, _vp, _i, _i, _vp]),
+    "qkv_prefill": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp],
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class QKVError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libqkv error {code}: {msg}")
+        self.code = code
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libqkv.so once; raise if it is absent (there is no other implementation)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(path):
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python -m chad_b200.build` "
+                    "(the quantized-KV attention path has no non-CUDA implementation)")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != QKV_OK:
+        msg = load().qkv_last_error()
+        raise QKVError(rc, msg.decode() if msg else "")

@@ -1,0 +1,268 @@
+// C-ABI entry points of libqkv.so: argument validation, kernel dispatch, error reporting.
+// Every entry point returns a status and never aborts; kernels are only enqueued on the
+// caller's stream (no allocation, no device synchronization) except qkv_device_status.
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <algorithm>
+
+#include "../../include/qkv.h"
+#include "qkv_internal.h"
+
+namespace qkv {
+
+__device__ int g_device_status = 0;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_check(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(QKV_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return QKV_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int* status_ptr() {
+  // Address of the device status word on the current device, looked up once per device.
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+int check_cache_shape(int D, int bits, int group_size) {
+  if (bits != 4 && bits != 8) return fail(QKV_EUNSUPPORTED, "bits must be 4 or 8 (got %d)", bits);
+  if (group_size != 64)
+    return fail(QKV_EUNSUPPORTED, "group_size must be 64 (got %d)", group_size);
+  if (D != 64 && D != 128 && D != 256)
+    return fail(QKV_EUNSUPPORTED, "head_dim must be 64, 128 or 256 (got %d)", D);
+  return QKV_OK;
+}
+
+}  // namespace
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+}  // namespace qkv
+
+using namespace qkv;
+
+extern "C" {
+
+int qkv_version(void) { return 100; }
+
+const char* qkv_last_error(void) { return g_err; }
+
+int qkv_device_status(void* stream, int reset) {
+  int* p = status_ptr();
+  if (!p) return fail(QKV_ECUDA, "device status word unavailable");
+  int v = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return cuda_check("qkv_device_status");
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyAsync(p, &zero, sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return cuda_check("qkv_device_status reset");
+  }
+  return v;
+}
+
+int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void* biases, int B,
+                        int H, int S, int D, int NP, int offset, int bits, int group_size,
+                        int scale_dtype, void* stream) {
+  int rc = check_cache_shape(D, bits, group_size);
+  if (rc) return rc;
+  if (!x || !w || !scales || !biases) return fail(QKV_EINVAL, "null pointer");
+  if (B < 0 || H < 0 || S < 0 || offset < 0 || NP < 0)
+    return fail(QKV_EINVAL, "negative size");
+  if ((long long)offset + S > NP)
+    return fail(QKV_EINVAL, "offset %d + S %d exceeds padded length %d", offset, S, NP);
+  if (x_dtype != QKV_BF16 && x_dtype != QKV_F16 && x_dtype != QKV_F32)
+    return fail(QKV_EINVAL, "bad x_dtype %d", x_dtype);
+  if (scale_dtype != QKV_BF16 && scale_dtype != QKV_F16)
+    return fail(QKV_EINVAL, "bad scale_dtype %d", scale_dtype);
+  rc = launch_quantize(x, x_dtype, w, scales, biases, B, H, S, D, NP, offset, bits, scale_dtype,
+                       static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "quantize: unsupported shape");
+  return cuda_check("qkv_quantize_append");
+}
+
+int qkv_dequantize(const void* w, const void* scales, const void* biases, void* out,
+                   long long rows, int D, int bits, int group_size, int dtype, int round_mode,
+                   void* stream) {
+  int rc = check_cache_shape(D, bits, group_size);
+  if (rc) return rc;
+  if (rows < 0) return fail(QKV_EINVAL, "negative rows");
+  if (!w || !scales || !biases || !out) return fail(QKV_EINVAL, "null pointer");
+  if (dtype != QKV_BF16 && dtype != QKV_F16) return fail(QKV_EINVAL, "bad dtype %d", dtype);
+  if (round_mode != 0 && round_mode != 1) return fail(QKV_EINVAL, "bad round_mode %d", round_mode);
+  rc = launch_dequantize(w, scales, biases, out, rows, D, bits, dtype, round_mode,
+                         static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "dequantize: unsupported shape");
+  return cuda_check("qkv_dequantize");
+}
+
+size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int bits,
+                          int group_size) {
+  (void)bits;
+  (void)group_size;
+  if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || D <= 0 || HQ % HKV) return 0;
+  const int R = (HQ / HKV) * S;
+  const int rg = (R + decode_rows_per_group(R) - 1) / decode_rows_per_group(R);
+  int splits = 1, chunk = kDecodeStagePos;
+  decode_pick_split(B, HKV, rg, std::max(n_max, 1), &splits, &chunk);
+  return decode_workspace_bytes(B, HQ, HKV, S, D, splits);
+}
+
+int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb, const void* vw,
+                  const void* vs, const void* vb, void* out, int B, int HQ, int HKV, int S, int D,
+                  int NP, int n, const int* lens, const int* pos_base, const int* total_lens,
+                  int bits, int group_size, int dtype, float scale, int mask_kind,
+                  const void* mask, int mask_nk, long long mask_sb, long long mask_sh,
+                  long long mask_sq, int out_kind, int splits, void* workspace, size_t ws_bytes,
+                  void* stream) {
+  int rc = check_cache_shape(D, bits, group_size);
+  if (rc) return rc;
+  if (!q || !kw || !ks || !kb || !vw || !vs || !vb || !out)
+    return fail(QKV_EINVAL, "null tensor pointer");
+  if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || NP < 0 || n < 0)
+    return fail(QKV_EINVAL, "bad sizes B=%d HQ=%d HKV=%d S=%d NP=%d n=%d", B, HQ, HKV, S, NP, n);
+  if (HQ % HKV) return fail(QKV_EINVAL, "HQ %d is not a multiple of HKV %d", HQ, HKV);
+  if (!lens && n > NP) return fail(QKV_EINVAL, "n %d exceeds padded length %d", n, NP);
+  if (NP % 8) return fail(QKV_EALIGN, "padded length %d must be a multiple of 8", NP);
+  if (!aligned16(q) || !aligned16(kw) || !aligned16(ks) || !aligned16(kb) || !aligned16(vw) ||
+      !aligned16(vs) || !aligned16(vb) || !aligned16(out))
+    return fail(QKV_EALIGN, "tensor pointers must be 16-byte aligned");
+  if (dtype != QKV_BF16 && dtype != QKV_F16) return fail(QKV_EINVAL, "bad dtype %d", dtype);
+  if (mask_kind < QKV_MASK_NONE || mask_kind > QKV_MASK_ADDITIVE)
+    return fail(QKV_EINVAL, "bad mask kind %d", mask_kind);
+  if ((mask_kind == QKV_MASK_BOOL || mask_kind == QKV_MASK_ADDITIVE) && (!mask || mask_nk <= 0))
+    return fail(QKV_EINVAL, "mask array missing");
+  if (out_kind != QKV_OUT_NORMALIZED && out_kind != QKV_OUT_PARTIAL)
+    return fail(QKV_EINVAL, "bad out_kind %d", out_kind);
+  if (splits < 0) return fail(QKV_EINVAL, "negative split count");
+
+  AttnArgs a{};
+  a.q = q;
+  a.kw = kw;
+  a.ks = ks;
+  a.kb = kb;
+  a.vw = vw;
+  a.vs = vs;
+  a.vb = vb;
+  a.out = out;
+  a.B = B;
+  a.HQ = HQ;
+  a.HKV = HKV;
+  a.S = S;
+  a.D = D;
+  a.NP = NP;
+  a.n = lens ? std::min(n, NP) : n;
+  a.lens = lens;
+  a.pos_base = pos_base;
+  a.total_lens = total_lens;
+  a.bits = bits;
+  a.dtype = dtype;
+  a.scale = scale;
+  // causal with one query token hides nothing: query S-1 sits at the last key
+  a.mask_kind = (mask_kind == QKV_MASK_CAUSAL && S == 1 && !pos_base && !total_lens)
+                    ? QKV_MASK_NONE
+                    : mask_kind;
+  a.mask = mask;
+  a.mask_nk = mask_nk;
+  a.mask_sb = mask_sb;
+  a.mask_sh = mask_sh;
+  a.mask_sq = mask_sq;
+  a.out_kind = out_kind;
+  a.status = status_ptr();
+
+  const int n_max = std::max(a.n, 1);
+  const int R = (HQ / HKV) * S;
+  const int rg = (R + decode_rows_per_group(R) - 1) / decode_rows_per_group(R);
+  if (splits == 0) {
+    decode_pick_split(B, HKV, rg, n_max, &a.splits, &a.chunk);
+  } else {
+    int ch = (n_max + splits - 1) / splits;
+    ch = std::max(kDecodeStagePos, (ch + kDecodeStagePos - 1) / kDecodeStagePos * kDecodeStagePos);
+    a.chunk = ch;
+    a.splits = std::max(1, (n_max + ch - 1) / ch);
+  }
+  const size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits);
+  if (!workspace || ws_bytes < need)
+    return fail(QKV_EWORKSPACE, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (!aligned16(workspace)) return fail(QKV_EALIGN, "workspace must be 16-byte aligned");
+  a.workspace = workspace;
+  a.ws_bytes = ws_bytes;
+
+  rc = launch_decode(a, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "attention: unsupported configuration");
+  return cuda_check("qkv_attention");
+}
+
+int qkv_combine(const float* parts, int n_parts, long long rows, int D, void* out, int out_dtype,
+                int out_kind, void* stream) {
+  if (!parts || !out) return fail(QKV_EINVAL, "null pointer");
+  if (n_parts <= 0 || rows < 0) return fail(QKV_EINVAL, "bad sizes");
+  if (D != 64 && D != 128 && D != 256) return fail(QKV_EUNSUPPORTED, "head_dim %d", D);
+  if (out_dtype != QKV_BF16 && out_dtype != QKV_F16) return fail(QKV_EINVAL, "bad dtype");
+  if (out_kind != QKV_OUT_NORMALIZED && out_kind != QKV_OUT_PARTIAL)
+    return fail(QKV_EINVAL, "bad out_kind %d", out_kind);
+  const int rc =
+      launch_combine(parts, n_parts, rows, rows, D, out, out_dtype, out_kind,
+                     static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "combine: unsupported");
+  return cuda_check("qkv_combine");
+}
+
+int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, void* ks, void* kb,
+                void* vw, void* vs, void* vb, void* out, int B, int HQ, int HKV, int S, int D,
+                int NP, int offset, int bits, int group_size, int dtype, float scale,
+                void* workspace, size_t ws_bytes, void* stream) {
+  if (!k_new || !v_new) return fail(QKV_EINVAL, "null new-token K/V");
+  int rc = qkv_quantize_append(k_new, dtype, kw, ks, kb, B, HKV, S, D, NP, offset, bits,
+                               group_size, dtype, stream);
+  if (rc) return rc;
+  rc = qkv_quantize_append(v_new, dtype, vw, vs, vb, B, HKV, S, D, NP, offset, bits, group_size,
+                           dtype, stream);
+  if (rc) return rc;
+  return qkv_attention(q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, offset + S, nullptr,
+                       nullptr, nullptr, bits, group_size, dtype, scale, QKV_MASK_CAUSAL, nullptr,
+                       0, 0, 0, 0, QKV_OUT_NORMALIZED, 0, workspace, ws_bytes, stream);
+}
+
+}  // extern "C"

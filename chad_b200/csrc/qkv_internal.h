@@ -1,0 +1,57 @@
+// Internal launch interface shared by the kernel translation units and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace qkv {
+
+// Everything one attention launch needs (device pointers; sizes already validated).
+struct AttnArgs {
+  const void* q;
+  const void* kw;
+  const void* ks;
+  const void* kb;
+  const void* vw;
+  const void* vs;
+  const void* vb;
+  void* out;
+  int B, HQ, HKV, S, D, NP;
+  int n;                 // key count when lens == nullptr
+  const int* lens;       // device int32[B] or nullptr
+  const int* pos_base;   // device int32[B] or nullptr
+  const int* total_lens; // device int32[B] or nullptr
+  int bits;
+  int dtype;  // QKV_BF16 / QKV_F16 (q, out, scales, biases, additive mask)
+  float scale;
+  int mask_kind;
+  const void* mask;
+  int mask_nk;
+  long long mask_sb, mask_sh, mask_sq;
+  int out_kind;
+  int splits;  // resolved split count (>= 1)
+  int chunk;   // keys per split (multiple of the stage size)
+  void* workspace;
+  size_t ws_bytes;
+  int* status;  // device status word for bounded-wait failures
+};
+
+// Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
+constexpr int kDecodeStagePos = 64;  // keys per pipeline stage
+int decode_rows_per_group(int R);    // query rows handled by one CTA (8 or 16)
+size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits);
+void decode_pick_split(int B, int HKV, int row_groups, int n_max, int* splits, int* chunk);
+int launch_decode(const AttnArgs& a, cudaStream_t st);
+
+int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
+                   int D, void* out, int out_dtype, int out_kind, cudaStream_t st);
+
+int launch_quantize(const void* x, int x_dtype, void* w, void* sc, void* bi, int B, int H,
+                    int S, int D, int NP, int offset, int bits, int scale_dtype,
+                    cudaStream_t st);
+int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, long long rows,
+                      int D, int bits, int dtype, int round_mode, cudaStream_t st);
+
+int num_sms();
+
+}  // namespace qkv

@@ -1,0 +1,209 @@
+// Affine quantize-on-append and dequantize for the MLX-layout KV cache (sm_100a).
+//
+// quantize: one warp per row of D values; the 64-value groups reduce min/max with warp
+// shuffles and every lane packs its own codes, so a row is read once and written once.
+// The arithmetic is float32 IEEE (no fast-math): max/min, (max-min)/(2^bits-1) clamped to
+// 1e-7, sign and edge from the larger-magnitude end, q0 = rint(edge/scale), then
+// scale = edge/q0 and bias = edge unless q0 == 0, codes = clamp(rint((x-bias)/scale)).
+// This is MLX's affine quantization as mlx-lm's QuantizedKVCache applies it before the
+// reference's attention (tests/test_mlx_qsdpa.py:45-49).
+#include "qkv_common.cuh"
+#include "qkv_internal.h"
+
+namespace qkv {
+
+template <typename TIn>
+__device__ __forceinline__ float load_as_f32(const TIn* p);
+template <>
+__device__ __forceinline__ float load_as_f32<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load_as_f32<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+template <>
+__device__ __forceinline__ float load_as_f32<__half>(const __half* p) { return __half2float(*p); }
+
+// E = D/32 values per lane (2, 4 or 8); group of 64 = 64/E lanes.
+template <typename TIn, typename TS, int BITS, int D>
+__global__ void __launch_bounds__(128) quantize_rows_kernel(const TIn* __restrict__ x,
+                                                            uint32_t* __restrict__ w,
+                                                            TS* __restrict__ scales,
+                                                            TS* __restrict__ biases, int H, int S,
+                                                            int NP, int offset, long long n_rows) {
+  constexpr int E = D / 32;
+  constexpr int LPG = 64 / E;  // lanes per group
+  constexpr int WPR = D * BITS / 32;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  // row = ((b*H + h)*S + s); destination position offset + s of the (b,h) slab
+  const long long bh = row / S;
+  const int s = (int)(row - bh * S);
+  const long long drow = bh * NP + offset + s;
+
+  float v[E];
+  const TIn* src = x + row * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = load_as_f32<TIn>(src + e);
+
+  float mx = v[0], mn = v[0];
+#pragma unroll
+  for (int e = 1; e < E; ++e) {
+    mx = fmaxf(mx, v[e]);
+    mn = fminf(mn, v[e]);
+  }
+#pragma unroll
+  for (int o = 1; o < LPG; o <<= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+  }
+  const float n_bins = float((1 << BITS) - 1);
+  float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), n_bins), 1e-7f);
+  const bool side = fabsf(mn) > fabsf(mx);
+  scale = side ? scale : -scale;
+  const float edge = side ? mn : mx;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  float bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
+
+  // pack this lane's E codes at bit offset (lane*E*BITS) % 32 of word (lane*E*BITS)/32
+  uint32_t part[(E * BITS + 31) / 32];
+#pragma unroll
+  for (int i = 0; i < (E * BITS + 31) / 32; ++i) part[i] = 0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    float c = rintf(__fdiv_rn(__fsub_rn(v[e], bias), scale));
+    c = fminf(fmaxf(c, 0.0f), n_bins);
+    const int bit = e * BITS;
+    part[bit / 32] |= uint32_t(c) << (bit % 32);
+  }
+  uint32_t* wrow = w + drow * WPR;
+  if constexpr (E * BITS >= 32) {
+#pragma unroll
+    for (int i = 0; i < E * BITS / 32; ++i) wrow[lane * (E * BITS / 32) + i] = part[i];
+  } else {
+    // several lanes share one word: OR their disjoint bit fields together
+    constexpr int LPW = 32 / (E * BITS);
+    uint32_t word = part[0] << ((lane % LPW) * E * BITS);
+#pragma unroll
+    for (int o = 1; o < LPW; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+    if (lane % LPW == 0) wrow[lane / LPW] = word;
+  }
+  if (lane % LPG == 0) {
+    const int grp = lane / LPG;
+    scales[drow * (D / 64) + grp] = Elem<TS>::from_f32(scale);
+    biases[drow * (D / 64) + grp] = Elem<TS>::from_f32(bias);
+  }
+}
+
+// One thread per packed word: 32/BITS outputs.
+template <typename TS, int BITS>
+__global__ void dequantize_kernel(const uint32_t* __restrict__ w, const TS* __restrict__ scales,
+                                  const TS* __restrict__ biases, TS* __restrict__ out,
+                                  long long n_words, int words_per_row, int groups_per_row,
+                                  int round_mode) {
+  constexpr int PER = 32 / BITS;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_words) return;
+  const long long row = i / words_per_row;
+  const int wi = (int)(i - row * words_per_row);
+  const int grp = wi * PER / 64;
+  const float s = Elem<TS>::to_f32(scales[row * groups_per_row + grp]);
+  const float b = Elem<TS>::to_f32(biases[row * groups_per_row + grp]);
+  const uint32_t word = w[i];
+  TS vals[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const float c = float((word >> (e * BITS)) & ((1u << BITS) - 1));
+    if (round_mode == 0) {
+      vals[e] = Elem<TS>::from_f32(__fmaf_rn(s, c, b));
+    } else {
+      const float m = Elem<TS>::to_f32(Elem<TS>::from_f32(__fmul_rn(s, c)));
+      vals[e] = Elem<TS>::from_f32(__fadd_rn(m, b));
+    }
+  }
+  TS* dst = out + i * PER;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) dst[e] = vals[e];
+}
+
+template <typename TIn, typename TS, int BITS>
+static int launch_quantize_d(const void* x, void* w, void* sc, void* bi, int B, int H, int S,
+                             int D, int NP, int offset, cudaStream_t st) {
+  const long long rows = (long long)B * H * S;
+  const int warps = 4;
+  const unsigned grid = (unsigned)((rows + warps - 1) / warps);
+#define QKV_Q_CASE(DD)                                                                   \
+  case DD:                                                                               \
+    quantize_rows_kernel<TIn, TS, BITS, DD><<<grid, warps * 32, 0, st>>>(                \
+        (const TIn*)x, (uint32_t*)w, (TS*)sc, (TS*)bi, H, S, NP, offset, rows);          \
+    break;
+  switch (D) {
+    QKV_Q_CASE(64)
+    QKV_Q_CASE(128)
+    QKV_Q_CASE(256)
+    default:
+      return QKV_EUNSUPPORTED;
+  }
+#undef QKV_Q_CASE
+  return QKV_OK;
+}
+
+template <typename TIn, typename TS>
+static int launch_quantize_b(const void* x, void* w, void* sc, void* bi, int B, int H, int S,
+                             int D, int NP, int offset, int bits, cudaStream_t st) {
+  if (bits == 4) return launch_quantize_d<TIn, TS, 4>(x, w, sc, bi, B, H, S, D, NP, offset, st);
+  return launch_quantize_d<TIn, TS, 8>(x, w, sc, bi, B, H, S, D, NP, offset, st);
+}
+
+int launch_quantize(const void* x, int x_dtype, void* w, void* sc, void* bi, int B, int H,
+                    int S, int D, int NP, int offset, int bits, int scale_dtype,
+                    cudaStream_t st) {
+  if (B * (long long)H * S == 0) return QKV_OK;
+  if (scale_dtype == QKV_BF16) {
+    if (x_dtype == QKV_BF16)
+      return launch_quantize_b<__nv_bfloat16, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+    if (x_dtype == QKV_F16)
+      return launch_quantize_b<__half, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+    return launch_quantize_b<float, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+  }
+  if (x_dtype == QKV_BF16)
+    return launch_quantize_b<__nv_bfloat16, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+  if (x_dtype == QKV_F16)
+    return launch_quantize_b<__half, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+  return launch_quantize_b<float, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+}
+
+int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, long long rows,
+                      int D, int bits, int dtype, int round_mode, cudaStream_t st) {
+  const int wpr = D * bits / 32;
+  const long long n_words = rows * wpr;
+  if (n_words == 0) return QKV_OK;
+  const int threads = 256;
+  const unsigned grid = (unsigned)((n_words + threads - 1) / threads);
+  if (dtype == QKV_BF16) {
+    if (bits == 4)
+      dequantize_kernel<__nv_bfloat16, 4><<<grid, threads, 0, st>>>(
+          (const uint32_t*)w, (const __nv_bfloat16*)sc, (const __nv_bfloat16*)bi,
+          (__nv_bfloat16*)out, n_words, wpr, D / 64, round_mode);
+    else
+      dequantize_kernel<__nv_bfloat16, 8><<<grid, threads, 0, st>>>(
+          (const uint32_t*)w, (const __nv_bfloat16*)sc, (const __nv_bfloat16*)bi,
+          (__nv_bfloat16*)out, n_words, wpr, D / 64, round_mode);
+  } else {
+    if (bits == 4)
+      dequantize_kernel<__half, 4><<<grid, threads, 0, st>>>(
+          (const uint32_t*)w, (const __half*)sc, (const __half*)bi, (__half*)out, n_words, wpr,
+          D / 64, round_mode);
+    else
+      dequantize_kernel<__half, 8><<<grid, threads, 0, st>>>(
+          (const uint32_t*)w, (const __half*)sc, (const __half*)bi, (__half*)out, n_words, wpr,
+          D / 64, round_mode);
+  }
+  return QKV_OK;
+}
+
+}  // namespace qkv

@@ -1,0 +1,244 @@
+"""Torch-tensor front end of the C ABI (libqkv.so).
+
+Tensors only carry device memory and streams here: every function passes raw pointers to
+the CUDA library and enqueues on torch's current stream.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence, Tuple, Union
+
+import torch
+
+from . import _lib
+from ._lib import check
+
+GROUP_SIZE = 64
+_DT = {torch.bfloat16: _lib.QKV_BF16, torch.float16: _lib.QKV_F16, torch.float32: _lib.QKV_F32}
+
+QuantTuple = Tuple[torch.Tensor, torch.Tensor, torch.Tensor]
+
+
+def dtype_code(t: Union[torch.Tensor, torch.dtype]) -> int:
+    dt = t.dtype if isinstance(t, torch.Tensor) else t
+    if dt not in _DT:
+        raise TypeError(f"unsupported dtype {dt}")
+    return _DT[dt]
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("libqkv operates on CUDA tensors only")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("tensors are on different devices")
+    return dev
+
+
+def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+# --------------------------------------------------------------------------------------
+# quantization
+# --------------------------------------------------------------------------------------
+
+def quantize_append(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                    biases: torch.Tensor, offset: int, bits: int,
+                    group_size: int = GROUP_SIZE) -> None:
+    """Quantize x (B, H, S, D) into the padded cache buffers at positions [offset, offset+S)."""
+    dev = _need_cuda(x, w, scales, biases)
+    _contig(x, "x"), _contig(w, "w"), _contig(scales, "scales"), _contig(biases, "biases")
+    b, h, s, d = x.shape
+    np_ = w.shape[2]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        check(lib.qkv_quantize_append(x.data_ptr(), dtype_code(x), w.data_ptr(),
+                                      scales.data_ptr(), biases.data_ptr(), b, h, s, d, np_,
+                                      offset, bits, group_size, dtype_code(scales),
+                                      _stream(dev)))
+
+
+def quantize(x: torch.Tensor, bits: int, group_size: int = GROUP_SIZE,
+             scale_dtype: Optional[torch.dtype] = None) -> QuantTuple:
+    """mx.quantize equivalent on the GPU: (w uint32, scales, biases) for x (..., D)."""
+    *lead, d = x.shape
+    rows = int(math.prod(lead)) if lead else 1
+    sd = scale_dtype or (x.dtype if x.dtype != torch.float32 else torch.bfloat16)
+    x4 = x.reshape(1, 1, rows, d).contiguous()
+    w = torch.empty((1, 1, rows, d * bits // 32), dtype=torch.int32, device=x.device)
+    sc = torch.empty((1, 1, rows, d // group_size), dtype=sd, device=x.device)
+    bi = torch.empty_like(sc)
+    quantize_append(x4, w, sc, bi, 0, bits, group_size)
+    return (w.view(*lead, -1), sc.view(*lead, -1), bi.view(*lead, -1))
+
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits: int,
+               group_size: int = GROUP_SIZE, round_mode: int = 0) -> torch.Tensor:
+    """mx.dequantize equivalent: values in the scale dtype, shape (..., D)."""
+    dev = _need_cuda(w, scales, biases)
+    d = w.shape[-1] * 32 // bits
+    rows = w.numel() // w.shape[-1]
+    out = torch.empty((*w.shape[:-1], d), dtype=scales.dtype, device=w.device)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        check(lib.qkv_dequantize(_contig(w, "w").data_ptr(), _contig(scales, "scales").data_ptr(),
+                                 _contig(biases, "biases").data_ptr(), out.data_ptr(), rows, d,
+                                 bits, group_size, dtype_code(scales), round_mode, _stream(dev)))
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# attention
+# --------------------------------------------------------------------------------------
+
+_WS = {}
+
+
+def workspace_size(B: int, HQ: int, HKV: int, S: int, D: int, n_max: int, bits: int,
+                   group_size: int = GROUP_SIZE) -> int:
+    return int(_lib.load().qkv_workspace_size(B, HQ, HKV, S, D, n_max, bits, group_size))
+
+
+def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (dev.type, dev.index)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = ws
+    return ws
+
+
+def _mask_args(mask, q: torch.Tensor, n_keys: int):
+    """-> (kind, tensor or None, mask_nk, sb, sh, sq)."""
+    if mask is None:
+        return _lib.QKV_MASK_NONE, None, 0, 0, 0, 0
+    if isinstance(mask, str):
+        if mask != "causal":
+            raise ValueError(f"unknown mask {mask!r}")
+        return _lib.QKV_MASK_CAUSAL, None, 0, 0, 0, 0
+    m = mask
+    if m.dtype == torch.bool:
+        m = m.to(torch.uint8)
+        kind = _lib.QKV_MASK_BOOL
+    else:
+        m = m.to(q.dtype)
+        kind = _lib.QKV_MASK_ADDITIVE
+    while m.dim() < 4:
+        m = m.unsqueeze(0)
+    if m.stride(-1) != 1:
+        m = m.contiguous()
+    b, hq, s, _ = q.shape
+    sb = m.stride(0) if m.shape[0] > 1 else 0
+    sh = m.stride(1) if m.shape[1] > 1 else 0
+    sq = m.stride(2) if m.shape[2] > 1 else 0
+    if (m.shape[0] not in (1, b)) or (m.shape[1] not in (1, hq)) or (m.shape[2] not in (1, s)):
+        raise ValueError(f"mask shape {tuple(mask.shape)} does not broadcast to {(b, hq, s, n_keys)}")
+    if m.shape[3] < n_keys:
+        raise ValueError(f"mask covers {m.shape[3]} keys < {n_keys}")
+    return kind, m, m.shape[3], sb, sh, sq
+
+
+def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequence[torch.Tensor],
+              scale: float, n: int, bits: int, *, lens: Optional[torch.Tensor] = None,
+              mask=None, out: Optional[torch.Tensor] = None, out_kind: int = 0,
+              pos_base: Optional[torch.Tensor] = None, total_lens: Optional[torch.Tensor] = None,
+              splits: int = 0, group_size: int = GROUP_SIZE,
+              workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of q (B, HQ, S, D) over full padded cache tuples (w, scales, biases).
+
+    n: valid key count (the upper bound of `lens` when per-batch lengths are given).
+    out_kind 0 returns (B, HQ, S, D) in q's dtype; 1 returns fp32 partial rows
+    (B, HQ, S, D+4) = [out(D), max (log2 units), sum, 0, 0].
+    """
+    kw, ks, kb = k_quant
+    vw, vs, vb = v_quant
+    dev = _need_cuda(q, kw, ks, kb, vw, vs, vb, lens, pos_base, total_lens)
+    for t, nm in ((q, "q"), (kw, "kw"), (ks, "ks"), (kb, "kb"), (vw, "vw"), (vs, "vs"), (vb, "vb")):
+        _contig(t, nm)
+    B, HQ, S, D = q.shape
+    HKV, NP = kw.shape[1], kw.shape[2]
+    if out is None:
+        if out_kind == _lib.QKV_OUT_NORMALIZED:
+            out = torch.empty_like(q)
+        else:
+            out = torch.empty((B, HQ, S, D + 4), dtype=torch.float32, device=q.device)
+    kind, m, mnk, sb, sh, sq = _mask_args(mask, q, n)
+    for t in (lens, pos_base, total_lens):
+        if t is not None and t.dtype != torch.int32:
+            raise TypeError("lens/pos_base/total_lens must be int32")
+    lib = _lib.load()
+    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size)
+    if splits:
+        need = max(need, splits * B * HQ * S * (D + 4) * 4 + (1 << 16))
+    ws = workspace if workspace is not None else _workspace(dev, need)
+    with torch.cuda.device(dev):
+        check(lib.qkv_attention(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
+                                vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(),
+                                B, HQ, HKV, S, D, NP, n, _ptr(lens), _ptr(pos_base),
+                                _ptr(total_lens), bits, group_size, dtype_code(q), float(scale),
+                                kind, _ptr(m), mnk, sb, sh, sq, out_kind, splits,
+                                ws.data_ptr(), ws.numel(), _stream(dev)))
+    return out
+
+
+def combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+            out_kind: int = 0) -> torch.Tensor:
+    """LSE-merge partial rows: parts (P, rows..., D+4) fp32 -> (rows..., D) or a merged partial."""
+    dev = _need_cuda(parts)
+    _contig(parts, "parts")
+    p = parts.shape[0]
+    d = parts.shape[-1] - 4
+    rows = parts[0].numel() // (d + 4)
+    if out_kind == _lib.QKV_OUT_NORMALIZED:
+        out = torch.empty((*parts.shape[1:-1], d), dtype=out_dtype, device=parts.device)
+    else:
+        out = torch.empty(parts.shape[1:], dtype=torch.float32, device=parts.device)
+    with torch.cuda.device(dev):
+        check(_lib.load().qkv_combine(parts.data_ptr(), p, rows, d, out.data_ptr(),
+                                      dtype_code(out_dtype), out_kind, _stream(dev)))
+    return out
+
+
+def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+            k_quant: Sequence[torch.Tensor], v_quant: Sequence[torch.Tensor], offset: int,
+            bits: int, scale: float, group_size: int = GROUP_SIZE) -> torch.Tensor:
+    """Quantize-append the new chunk at [offset, offset+S) then attend causally over all keys."""
+    kw, ks, kb = k_quant
+    vw, vs, vb = v_quant
+    dev = _need_cuda(q, k_new, v_new, kw)
+    B, HQ, S, D = q.shape
+    HKV, NP = kw.shape[1], kw.shape[2]
+    out = torch.empty_like(q)
+    need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size)
+    ws = _workspace(dev, need)
+    with torch.cuda.device(dev):
+        check(_lib.load().qkv_prefill(
+            _contig(q, "q").data_ptr(), _contig(k_new, "k_new").data_ptr(),
+            _contig(v_new, "v_new").data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
+            vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B, HQ, HKV, S, D, NP,
+            offset, bits, group_size, dtype_code(q), float(scale), ws.data_ptr(), ws.numel(),
+            _stream(dev)))
+    return out
+
+
+def device_status(reset: bool = True) -> int:
+    """Device status word (0 = no kernel gave up on a bounded wait). Synchronizes."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    return int(_lib.load().qkv_device_status(_stream(dev), 1 if reset else 0))
