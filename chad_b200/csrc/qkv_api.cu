@@ -149,13 +149,16 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
   return decode_workspace_bytes(B, HQ, HKV, S, D, splits);
 }
 
-int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb, const void* vw,
-                  const void* vs, const void* vb, void* out, int B, int HQ, int HKV, int S, int D,
-                  int NP, int n, const int* lens, const int* pos_base, const int* total_lens,
-                  int bits, int group_size, int dtype, float scale, int mask_kind,
-                  const void* mask, int mask_nk, long long mask_sb, long long mask_sh,
-                  long long mask_sq, int out_kind, int splits, void* workspace, size_t ws_bytes,
-                  void* stream) {
+namespace {
+
+// Validate and pack the shared arguments of qkv_attention / qkv_partials.
+int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const void* kb,
+               const void* vw, const void* vs, const void* vb, void* out, int B, int HQ,
+               int HKV, int S, int D, int NP, int n, const int* lens, const int* pos_base,
+               const int* total_lens, int bits, int group_size, int dtype, float scale,
+               int mask_kind, const void* mask, int mask_nk, long long mask_sb,
+               long long mask_sh, long long mask_sq, int splits, void* workspace,
+               size_t ws_bytes) {
   int rc = check_cache_shape(D, bits, group_size);
   if (rc) return rc;
   if (!q || !kw || !ks || !kb || !vw || !vs || !vb || !out)
@@ -173,11 +176,9 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
     return fail(QKV_EINVAL, "bad mask kind %d", mask_kind);
   if ((mask_kind == QKV_MASK_BOOL || mask_kind == QKV_MASK_ADDITIVE) && (!mask || mask_nk <= 0))
     return fail(QKV_EINVAL, "mask array missing");
-  if (out_kind != QKV_OUT_NORMALIZED && out_kind != QKV_OUT_PARTIAL)
-    return fail(QKV_EINVAL, "bad out_kind %d", out_kind);
   if (splits < 0) return fail(QKV_EINVAL, "negative split count");
 
-  AttnArgs a{};
+  a = AttnArgs{};
   a.q = q;
   a.kw = kw;
   a.ks = ks;
@@ -208,7 +209,6 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
   a.mask_sb = mask_sb;
   a.mask_sh = mask_sh;
   a.mask_sq = mask_sq;
-  a.out_kind = out_kind;
   a.status = status_ptr();
 
   const int n_max = std::max(a.n, 1);
@@ -228,10 +228,49 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
   if (!aligned16(workspace)) return fail(QKV_EALIGN, "workspace must be 16-byte aligned");
   a.workspace = workspace;
   a.ws_bytes = ws_bytes;
+  return QKV_OK;
+}
 
+}  // namespace
+
+int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb, const void* vw,
+                  const void* vs, const void* vb, void* out, int B, int HQ, int HKV, int S, int D,
+                  int NP, int n, const int* lens, const int* pos_base, const int* total_lens,
+                  int bits, int group_size, int dtype, float scale, int mask_kind,
+                  const void* mask, int mask_nk, long long mask_sb, long long mask_sh,
+                  long long mask_sq, int out_kind, int splits, void* workspace, size_t ws_bytes,
+                  void* stream) {
+  if (out_kind != QKV_OUT_NORMALIZED && out_kind != QKV_OUT_PARTIAL)
+    return fail(QKV_EINVAL, "bad out_kind %d", out_kind);
+  AttnArgs a;
+  int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, n, lens,
+                      pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
+                      mask_nk, mask_sb, mask_sh, mask_sq, splits, workspace, ws_bytes);
+  if (rc) return rc;
+  a.out_kind = out_kind;
   rc = launch_decode(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "attention: unsupported configuration");
   return cuda_check("qkv_attention");
+}
+
+int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, const void* vw,
+                 const void* vs, const void* vb, float* parts, size_t parts_bytes, int* n_parts,
+                 int B, int HQ, int HKV, int S, int D, int NP, int n, const int* lens,
+                 const int* pos_base, const int* total_lens, int bits, int group_size,
+                 int dtype, float scale, int mask_kind, const void* mask, int mask_nk,
+                 long long mask_sb, long long mask_sh, long long mask_sq, int splits,
+                 void* stream) {
+  if (!n_parts) return fail(QKV_EINVAL, "n_parts is null");
+  AttnArgs a;
+  int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, parts, B, HQ, HKV, S, D, NP, n, lens,
+                      pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
+                      mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes);
+  if (rc) return rc;
+  a.out_kind = QKV_OUT_PARTIAL;
+  *n_parts = a.splits;
+  rc = launch_split_only(a, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "partials: unsupported configuration");
+  return cuda_check("qkv_partials");
 }
 
 int qkv_combine(const float* parts, int n_parts, long long rows, int D, void* out, int out_dtype,

@@ -630,13 +630,15 @@ size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits) 
   return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
 }
 
-int launch_decode(const AttnArgs& a, cudaStream_t st) {
+int launch_split_only(const AttnArgs& a, cudaStream_t st) {
   const int R = (a.HQ / a.HKV) * a.S;
-  int rc;
   if (a.dtype == QKV_BF16)
-    rc = R <= 8 ? launch_split_b<__nv_bfloat16, 1>(a, st) : launch_split_b<__nv_bfloat16, 2>(a, st);
-  else
-    rc = R <= 8 ? launch_split_b<__half, 1>(a, st) : launch_split_b<__half, 2>(a, st);
+    return R <= 8 ? launch_split_b<__nv_bfloat16, 1>(a, st) : launch_split_b<__nv_bfloat16, 2>(a, st);
+  return R <= 8 ? launch_split_b<__half, 1>(a, st) : launch_split_b<__half, 2>(a, st);
+}
+
+int launch_decode(const AttnArgs& a, cudaStream_t st) {
+  const int rc = launch_split_only(a, st);
   if (rc != QKV_OK) return rc;
   const long long rows = (long long)a.B * a.HQ * a.S;
   return launch_combine((const float*)a.workspace, a.splits, rows, rows, a.D, a.out, a.dtype,

@@ -41,7 +41,8 @@ constexpr int kDecodeStagePos = 64;  // keys per pipeline stage
 int decode_rows_per_group(int R);    // query rows handled by one CTA (8 or 16)
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits);
 void decode_pick_split(int B, int HKV, int row_groups, int n_max, int* splits, int* chunk);
-int launch_decode(const AttnArgs& a, cudaStream_t st);
+int launch_decode(const AttnArgs& a, cudaStream_t st);  // split kernel + combine
+int launch_split_only(const AttnArgs& a, cudaStream_t st);  // partial rows into a.workspace
 
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
                    int D, void* out, int out_dtype, int out_kind, cudaStream_t st);

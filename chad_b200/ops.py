@@ -6,6 +6,7 @@ the CUDA library and enqueues on torch's current stream.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Optional, Sequence, Tuple, Union
 
@@ -196,6 +197,35 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
                                 kind, _ptr(m), mnk, sb, sh, sq, out_kind, splits,
                                 ws.data_ptr(), ws.numel(), _stream(dev)))
     return out
+
+
+def partials(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequence[torch.Tensor],
+             scale: float, n: int, bits: int, *, lens: Optional[torch.Tensor] = None,
+             mask=None, parts: Optional[torch.Tensor] = None, splits: int = 0,
+             pos_base: Optional[torch.Tensor] = None, total_lens: Optional[torch.Tensor] = None,
+             group_size: int = GROUP_SIZE) -> torch.Tensor:
+    """Pass 1 only: per-split partial rows (P, B, HQ, S, D+4) fp32, un-merged."""
+    kw, ks, kb = k_quant
+    vw, vs, vb = v_quant
+    dev = _need_cuda(q, kw, ks, kb, vw, vs, vb, lens, pos_base, total_lens)
+    B, HQ, S, D = q.shape
+    HKV, NP = kw.shape[1], kw.shape[2]
+    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size)
+    if splits:
+        need = max(need, splits * B * HQ * S * (D + 4) * 4 + (1 << 16))
+    if parts is None:
+        parts = torch.empty(need // 4, dtype=torch.float32, device=q.device)
+    kind, m, mnk, sb, sh, sq = _mask_args(mask, q, n)
+    np_out = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        check(_lib.load().qkv_partials(
+            q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(), vw.data_ptr(),
+            vs.data_ptr(), vb.data_ptr(), parts.data_ptr(), parts.numel() * parts.element_size(),
+            ctypes.byref(np_out), B, HQ, HKV, S, D, NP, n, _ptr(lens), _ptr(pos_base),
+            _ptr(total_lens), bits, group_size, dtype_code(q), float(scale), kind, _ptr(m), mnk,
+            sb, sh, sq, splits, _stream(dev)))
+    p = np_out.value
+    return parts.view(-1)[: p * B * HQ * S * (D + 4)].view(p, B, HQ, S, D + 4)
 
 
 def combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,

@@ -121,6 +121,22 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
                   int splits, void* workspace, size_t ws_bytes, void* stream);
 
 /*
+ * Pass 1 only: write the per-split partial rows of qkv_attention without merging them
+ * (the reference's pass-1 contract, src/chad/mlx_qsdpa.py:73-209: per block of keys the
+ * (max, sum, un-normalised output) of every query row). parts receives
+ * [*n_parts][B*HQ*S][D+4] floats, rows laid out as in QKV_OUT_PARTIAL; parts_bytes must be
+ * >= qkv_workspace_size(...) for these sizes. *n_parts (host int) receives the split count.
+ * Arguments otherwise as in qkv_attention. Merge with qkv_combine.
+ */
+int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb,
+                 const void* vw, const void* vs, const void* vb, float* parts,
+                 size_t parts_bytes, int* n_parts, int B, int HQ, int HKV, int S, int D,
+                 int NP, int n, const int* lens, const int* pos_base, const int* total_lens,
+                 int bits, int group_size, int dtype, float scale, int mask_kind,
+                 const void* mask, int mask_nk, long long mask_sb, long long mask_sh,
+                 long long mask_sq, int splits, void* stream);
+
+/*
  * Merge n_parts partial results (QKV_OUT_PARTIAL rows) per query row: the pass-2
  * log-sum-exp combine of src/chad/mlx_qsdpa.py:233-258, used to merge sequence shards
  * gathered from several GPUs. parts: float [n_parts][rows][D+4]; out: (rows, D) in

@@ -1,0 +1,93 @@
+"""libqkv.so loads, exports every symbol include/qkv.h declares, and rejects bad arguments
+with status codes before touching a GPU (so these run on CPU-only machines too)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from chad_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "qkv.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qkv_[a-z_]+)\s*\(", src)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("qkv_attention", "qkv_partials", "qkv_combine", "qkv_prefill",
+                 "qkv_quantize_append", "qkv_dequantize", "qkv_workspace_size",
+                 "qkv_last_error", "qkv_version", "qkv_device_status"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_workspace_size():
+    lib = _lib.load()
+    assert lib.qkv_version() == 100
+    assert lib.qkv_workspace_size(1, 32, 4, 1, 128, 32768, 4, 64) > 0
+    assert lib.qkv_workspace_size(1, 30, 4, 1, 128, 32768, 4, 64) == 0  # HQ % HKV
+
+
+def _attn(lib, **over):
+    a = dict(q=16, kw=16, ks=16, kb=16, vw=16, vs=16, vb=16, out=16, B=1, HQ=16, HKV=2, S=1,
+             D=128, NP=512, n=100, lens=None, pos_base=None, total_lens=None, bits=4, gs=64,
+             dtype=0, scale=0.1, mask_kind=0, mask=None, mask_nk=0, sb=0, sh=0, sq=0,
+             out_kind=0, splits=0, ws=16, ws_bytes=1 << 20, stream=None)
+    a.update(over)
+    return lib.qkv_attention(*a.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(bits=5), _lib.QKV_EUNSUPPORTED),
+    (dict(gs=32), _lib.QKV_EUNSUPPORTED),
+    (dict(D=96), _lib.QKV_EUNSUPPORTED),
+    (dict(q=None), _lib.QKV_EINVAL),
+    (dict(HQ=15), _lib.QKV_EINVAL),
+    (dict(n=600), _lib.QKV_EINVAL),
+    (dict(NP=500, n=100), _lib.QKV_EALIGN),
+    (dict(kw=18), _lib.QKV_EALIGN),
+    (dict(mask_kind=2), _lib.QKV_EINVAL),
+    (dict(mask_kind=7), _lib.QKV_EINVAL),
+    (dict(out_kind=3), _lib.QKV_EINVAL),
+    (dict(dtype=2), _lib.QKV_EINVAL),
+])
+def test_attention_rejects_bad_arguments(over, code):
+    lib = _lib.load()
+    assert _attn(lib, **over) == code
+    assert lib.qkv_last_error()  # a message was set
+
+
+def test_quantize_and_dequantize_reject_bad_arguments():
+    lib = _lib.load()
+    assert lib.qkv_quantize_append(16, 0, 16, 16, 16, 1, 2, 10, 128, 8, 0, 4, 64, 0, None) \
+        == _lib.QKV_EINVAL  # offset + S > NP
+    assert lib.qkv_quantize_append(16, 5, 16, 16, 16, 1, 2, 1, 128, 8, 0, 4, 64, 0, None) \
+        == _lib.QKV_EINVAL
+    assert lib.qkv_dequantize(16, 16, 16, 16, 4, 128, 3, 64, 0, 0, None) == _lib.QKV_EUNSUPPORTED
+    assert lib.qkv_dequantize(16, 16, 16, 16, 4, 128, 4, 64, 0, 2, None) == _lib.QKV_EINVAL
+    n = ctypes.c_int(0)
+    assert lib.qkv_partials(16, 16, 16, 16, 16, 16, 16, 16, 1 << 20, None, 1, 16, 2, 1, 128,
+                            512, 10, None, None, None, 4, 64, 0, 0.1, 0, None, 0, 0, 0, 0, 0,
+                            None) == _lib.QKV_EINVAL  # n_parts null
+    assert lib.qkv_combine(None, 2, 4, 128, 16, 0, 0, None) == _lib.QKV_EINVAL
+    assert n.value == 0
+
+
+def test_check_raises_with_message():
+    lib = _lib.load()
+    rc = lib.qkv_dequantize(16, 16, 16, 16, 4, 100, 4, 64, 0, 0, None)
+    with pytest.raises(_lib.QKVError) as e:
+        _lib.check(rc)
+    assert "head_dim" in str(e.value)
