@@ -53,6 +53,15 @@ SIGNATURES = {
          _i, _vp, _i, _ll, _ll, _ll,  # mask
          _i, _vp],  # splits stream
     ),
+    "qkv_attention_noalloc": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,  # q, kw, ks, kb, vw, vs, vb, out
+         _i, _i, _i, _i, _i, _i, _i,  # B HQ HKV S D NP n
+         _vp, _vp, _vp,  # lens pos_base total_lens
+         _i, _i, _i, _f,  # bits group_size dtype scale
+         _i, _vp, _i, _ll, _ll, _ll,  # mask_kind mask mask_nk strides
+         _i, _i, _vp],  # out_kind splits stream
+    ),
     "qkv_combine": (_i, [_vp, _i, _ll, _i, _vp, _i, _i, _vp]),
     "qkv_prefill": (
         _i,

@@ -75,6 +75,14 @@ int num_sms() {
   return cached[dev];
 }
 
+int set_last_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 }  // namespace qkv
 
 using namespace qkv;

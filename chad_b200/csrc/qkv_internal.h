@@ -55,4 +55,7 @@ int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, 
 
 int num_sms();
 
+// Record a message for qkv_last_error() on this thread and return `code`.
+int set_last_error(int code, const char* fmt, ...);
+
 }  // namespace qkv

@@ -156,6 +156,27 @@ int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, v
                 int S, int D, int NP, int offset, int bits, int group_size, int dtype,
                 float scale, void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * qkv_attention without a workspace argument, for callers that cannot allocate device
+ * memory (an FFI host with no CUDA allocator of its own, or an engine whose HBM is reserved
+ * up front by a fixed-budget pool). No counterpart in the reference: the reference's
+ * kernels allocate their outputs through MLX.
+ *
+ * The split partials live in a 4 MiB static scratch array inside libqkv.so (held on every
+ * GPU that loads the library, until exit); calls whose partials need more return
+ * QKV_EWORKSPACE with a message naming both sizes. The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress) and should come before any stream capture. All
+ * calls on a device share the array: calls that overlap on the GPU race, so serialize them.
+ * Arguments and results are those of qkv_attention.
+ */
+int qkv_attention_noalloc(const void* q, const void* kw, const void* ks, const void* kb,
+                          const void* vw, const void* vs, const void* vb, void* out, int B,
+                          int HQ, int HKV, int S, int D, int NP, int n, const int* lens,
+                          const int* pos_base, const int* total_lens, int bits,
+                          int group_size, int dtype, float scale, int mask_kind,
+                          const void* mask, int mask_nk, long long mask_sb, long long mask_sh,
+                          long long mask_sq, int out_kind, int splits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
