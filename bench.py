@@ -191,7 +191,7 @@ def run_ours(args, cfg, rank, world, device):
     part_local = torch.empty((L, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
     gathered = torch.empty((world, L, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
     ws_bytes = ops.workspace_size(B, HQ, HKV, 1, D, nloc, bits)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)  # counters start at zero
     keys_total = sum(loc)  # this rank's keys per layer (all batch rows)
     kv_bytes_rank = keys_total * HKV * kv_bytes_per_key(D, bits)
 

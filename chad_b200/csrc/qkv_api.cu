@@ -151,10 +151,11 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
   (void)group_size;
   if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || D <= 0 || HQ % HKV) return 0;
   const int R = (HQ / HKV) * S;
-  const int rg = (R + decode_rows_per_group(R) - 1) / decode_rows_per_group(R);
-  int splits = 1, chunk = kDecodeStagePos;
-  decode_pick_split(B, HKV, rg, std::max(n_max, 1), &splits, &chunk);
-  return decode_workspace_bytes(B, HQ, HKV, S, D, splits);
+  const int rg = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
+  (void)rg;
+  int splits = 1, chunk = 16, cluster = 1;
+  decode_plan(B, HQ, HKV, S, D, bits, std::max(n_max, 1), 0, &splits, &chunk, &cluster);
+  return decode_workspace_bytes(B, HQ, HKV, S, D, splits, cluster);
 }
 
 namespace {
@@ -171,7 +172,7 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
   if (rc) return rc;
   if (!q || !kw || !ks || !kb || !vw || !vs || !vb || !out)
     return fail(QKV_EINVAL, "null tensor pointer");
-  if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || NP < 0 || n < 0)
+  if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || NP <= 0 || n < 0)
     return fail(QKV_EINVAL, "bad sizes B=%d HQ=%d HKV=%d S=%d NP=%d n=%d", B, HQ, HKV, S, NP, n);
   if (HQ % HKV) return fail(QKV_EINVAL, "HQ %d is not a multiple of HKV %d", HQ, HKV);
   if (!lens && n > NP) return fail(QKV_EINVAL, "n %d exceeds padded length %d", n, NP);
@@ -218,19 +219,20 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
   a.mask_sh = mask_sh;
   a.mask_sq = mask_sq;
   a.status = status_ptr();
+  // The kernel issued just before an attention call may be the append of its S tokens
+  // (positions n-S..n-1); everything older is immutable during that kernel, so the attention
+  // kernel may start streaming it early (programmatic dependent launch). With per-batch
+  // lengths on the device nothing is read early.
+  a.prefetch_limit = lens ? 0 : std::max(0, std::min(n, NP) - S);
 
   const int n_max = std::max(a.n, 1);
   const int R = (HQ / HKV) * S;
-  const int rg = (R + decode_rows_per_group(R) - 1) / decode_rows_per_group(R);
-  if (splits == 0) {
-    decode_pick_split(B, HKV, rg, n_max, &a.splits, &a.chunk);
-  } else {
-    int ch = (n_max + splits - 1) / splits;
-    ch = std::max(kDecodeStagePos, (ch + kDecodeStagePos - 1) / kDecodeStagePos * kDecodeStagePos);
-    a.chunk = ch;
-    a.splits = std::max(1, (n_max + ch - 1) / ch);
-  }
-  const size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits);
+  const int rg = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
+  if ((long long)B * HKV * rg > kMaxCounters)
+    return fail(QKV_EUNSUPPORTED, "too many query-row groups (%lld > %d)",
+                (long long)B * HKV * rg, kMaxCounters);
+  decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
+  const size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
   if (!workspace || ws_bytes < need)
     return fail(QKV_EWORKSPACE, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (!aligned16(workspace)) return fail(QKV_EALIGN, "workspace must be 16-byte aligned");
@@ -275,7 +277,7 @@ int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, 
                       mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes);
   if (rc) return rc;
   a.out_kind = QKV_OUT_PARTIAL;
-  *n_parts = a.splits;
+  *n_parts = a.splits / a.cluster;
   rc = launch_split_only(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "partials: unsupported configuration");
   return cuda_check("qkv_partials");

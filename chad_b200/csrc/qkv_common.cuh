@@ -142,14 +142,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread (up to `ns`) until the phase flips,
+// instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (after flagging the device status) if the phase never flips.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
                                           int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kSpinNanos) break;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;  // suspend up to 0.1 ms
+    if (global_ns() - t0 > kSpinNanos) break;
   }
   flag_device_error(status, where);
   return false;

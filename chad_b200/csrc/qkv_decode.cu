@@ -3,29 +3,37 @@
 // Replaces the reference's pass 1 (`_P1_SRC`, src/chad/mlx_qsdpa.py:73-209, and its
 // simdgroup-matrix retile `_P1_SGM_SRC`, :303-473) and pass 2 (`_P2_SRC`, :213-265).
 //
-// Shape of the work. One CTA = one (batch b, kv head, query-row group, key split). Its
-// query rows are the GQA heads x query tokens that share the kv head (at most 16, stored
-// contiguously in q). A producer warp streams the split's keys through a 4-deep ring of
-// shared-memory stages with 1-D bulk async copies (TMA): per stage 64 keys of packed K and
-// V codes plus their scales and biases. Four consumer warps take 16 keys each per stage.
+// Work split. One CTA = one (batch b, kv head, query-row group, key split); its query rows
+// are the GQA heads x query tokens that share the kv head (at most 16, contiguous in q).
+// Consecutive splits of the same rows form a thread-block cluster (up to 8 CTAs).
 //
-// The tensor-core mapping is the reference's retile insight (keys share one dequantized
-// tile across the whole GQA group) turned around for mma.sync m16n8k16: the 16 KEYS are
-// the MMA's M rows and the query rows are its N columns, so GQA 8 fills an N=8 tile with
-// no padding.
-//   scores^T (16 keys x 8 rows)  = K (16 x D) . (q*scale*log2e)^T      D/16 MMAs
-//   out^T    (D x 8 rows)       += V^T (D x 16 keys) . P^T (16 x 8)    D/16 MMAs
-// K and V^T fragments are built straight from packed codes in registers: a code c becomes
-// the f16 value 1024+c by OR-ing it into the exponent pattern 0x6400 (exact), then
-// (x - 1024) * scale + bias with f16x2 FMAs. The score accumulator is turned into the
-// P^T operand with one movmatrix.trans per 8x8 block, so no shared-memory round trip is
-// needed between the two products.
+// Memory path. A producer warp streams 64-key stages into a shared-memory ring: K and V code
+// tiles with 2-D TMA tensor copies (swizzled so that every consumer read below is free of
+// bank conflicts) and the four scale/bias arrays with 1-D bulk copies, all completing on
+// mbarriers. No multicast.
 //
-// Online softmax runs in base 2 per query row (the row's 8 lanes reduce with three xor
-// shuffles) and the four warps' (max, sum, out) triples are merged through shared memory
-// at the end, so each CTA writes one partial per row: [out(D), max, sum, 0, 0] in fp32.
-// A combine kernel (the reference's pass 2) folds the splits.
+// Math. Four consumer warps take 16 keys each per stage and run mma.sync m16n8k16 with the
+// 16 KEYS as the M rows and the query rows as the N columns (GQA 8 fills N=8 exactly). The
+// packed codes are fed to the tensor cores as they are: AND-ing a 4-bit code into the low
+// bits of an f16 (or placing an 8-bit code there with PRMT) gives the subnormal f16 value
+// code * 2^-24 exactly, and B200's f16 MMA is exact on subnormal inputs. Because every
+// k-step of QK (and every m-tile of PV) stays inside one 64-wide scale group, the affine
+// parameters factor out of the products:
+//   score(key, row)  = sum_g s[key,g] * 2^24 * (codes_g . q_g)  +  sum_g b[key,g] * sum(q_g)
+//   out(dim g, row) += 2^24 * sum_key (p * s[key,g]) * code  +  sum_key p * b[key,g]
+// so no per-element dequantisation arithmetic is left: per code the kernel spends one
+// LOP3/PRMT (4-bit: one per two codes) and the tensor cores do the rest. P^T is built from
+// the score accumulator with movmatrix.trans (no shared-memory round trip).
+//
+// Reduction. Online softmax in base 2; the four warps merge through shared memory into one
+// CTA partial (out, max, sum); the CTAs of a cluster merge those through distributed shared
+// memory into one cluster partial in global memory; a combine kernel (the reference's pass
+// 2), chained by programmatic dependent launch, merges the cluster partials.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "qkv_common.cuh"
 #include "qkv_internal.h"
@@ -34,59 +42,73 @@ namespace qkv {
 
 namespace {
 
-constexpr int kWarps = 4;                  // consumer warps
+constexpr int kWarps = 4;                    // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
-constexpr int kTP = kDecodeStagePos;        // keys per stage (16 per consumer warp)
+constexpr int kBoxRows = 64;                 // key rows per TMA box
+constexpr int kMaxCluster = 8;
+constexpr int kMaxClustersPerGroup = 64;  // bounds the final merge's shared-memory tables
 #define kNegInf (-__int_as_float(0x7f800000))
 
+// Order in which the 16 keys of a warp tile occupy the MMA rows. The tables make the rows
+// that one shared-memory wavefront reads land in distinct bank windows of the swizzled tile
+// (64-byte rows / 64B swizzle for 4-bit D128, 128-byte rows / 128B swizzle for 8-bit).
 template <int BITS>
 __device__ __forceinline__ int key_perm(int k) {
-  // Order in which the 16 keys of a warp tile occupy the MMA rows. For 4-bit codes
-  // (64-byte rows) the order 0,3,1,2,4,7,5,6 (+8) makes the rows that one lane quarter
-  // reads together alternate between the two 64-byte halves of a bank cycle.
-  if constexpr (BITS == 4) {
-    const int lo = k & 3;
-    return (k & 12) | (lo == 0 ? 0 : lo == 1 ? 3 : lo - 1);
-  } else {
-    return k;
-  }
+  const int lo = k & 7;
+  const int p = BITS == 4 ? (0x76234510 >> (4 * lo)) & 7   // 0,1,5,4,3,2,6,7
+                          : (0x37156240 >> (4 * lo)) & 7;  // 0,4,2,6,5,1,7,3
+  return (k & 8) | p;
 }
 
-template <typename T, int BITS, int D>
-struct Cfg {
-  static constexpr int RB = D * BITS / 8;       // code bytes per key row
-  static constexpr int G = D / 64;              // scale groups per row
-  static constexpr int KCHUNK = RB / 4;         // K bytes per lane (its quarter of D)
-  static constexpr int VCHUNK = RB / 8;         // V bytes per lane (its eighth of D)
-  static constexpr int KS = D / 16;             // MMA k-steps of QK / m-tiles of PV
-  static constexpr int CODES_BYTES = kTP * RB;
-  static constexpr int SC_BYTES = kTP * G * 2;
+// 16-key sub-tiles per consumer warp per stage: two where registers allow, so a warp runs
+// two independent MMA chains and shares one softmax reduction between them.
+template <int D, int NT>
+constexpr int sub_tiles() { return (NT == 1 && D <= 128) ? 2 : 1; }
+
+template <int BITS, int D, int TP>
+struct Geo {
+  static constexpr int G = D / 64;                   // scale groups per row
+  static constexpr int RB = D * BITS / 8;            // code bytes per key
+  static constexpr int RBOX = RB < 128 ? RB : 128;   // TMA box inner bytes (swizzle span)
+  static constexpr int NBOX = RB / RBOX;             // boxes per code row
+  static constexpr int SWZ = RBOX == 128 ? 7 : RBOX == 64 ? 3 : 1;
+  static constexpr int GB = 64 * BITS / 8;           // code bytes of one scale group
+  static constexpr int KLB = 16 * BITS / 8;          // K bytes per lane per group per key
+  static constexpr int VLB = 8 * BITS / 8;           // V bytes per lane per group per key
+  static constexpr int KW = KLB / 4, VW = VLB / 4;   // words
+  static constexpr int CODE_BYTES = TP * RB;
+  static constexpr int SC_BYTES = TP * G * 2;
   static constexpr int OFF_KC = 0;
-  static constexpr int OFF_VC = CODES_BYTES;
-  static constexpr int OFF_KS = 2 * CODES_BYTES;
+  static constexpr int OFF_VC = CODE_BYTES;
+  static constexpr int OFF_KS = 2 * CODE_BYTES;
   static constexpr int OFF_KB = OFF_KS + SC_BYTES;
   static constexpr int OFF_VS = OFF_KB + SC_BYTES;
   static constexpr int OFF_VB = OFF_VS + SC_BYTES;
-  static constexpr int STAGE_BYTES = ((OFF_VB + SC_BYTES) + 127) / 128 * 128;
-  static constexpr int STAGES = STAGE_BYTES * 4 <= 96 * 1024 ? 4 : 3;
+  static constexpr int STAGE_BYTES = ((OFF_VB + SC_BYTES) + 1023) / 1024 * 1024;
+  static constexpr int STAGES = STAGE_BYTES * 4 <= 72 * 1024 ? 4
+                                : STAGE_BYTES * 3 <= 72 * 1024 ? 3 : 2;
 };
 
-__device__ __forceinline__ uint32_t u32_load_sh(const uint8_t* p) {
-  return *reinterpret_cast<const uint32_t*>(p);
+// Byte offset of (key row, code byte) inside a swizzled code tile.
+template <int BITS, int D, int TP>
+__device__ __forceinline__ int code_off(int key, int byte) {
+  using g = Geo<BITS, D, TP>;
+  const int sub = byte / g::RBOX;
+  const int lin = key * g::RBOX + (byte % g::RBOX);
+  return sub * (TP * g::RBOX) + (lin ^ (((lin >> 7) & g::SWZ) << 4));
 }
 
-// Load `N` bytes (8, 16, 32 or 64) of shared memory into words.
 template <int N>
-__device__ __forceinline__ void lds_bytes(uint32_t* dst, const uint8_t* src) {
-  if constexpr (N == 4) {
+__device__ __forceinline__ void lds_words(uint32_t* dst, const uint8_t* src) {
+  if constexpr (N == 1) {
     dst[0] = *reinterpret_cast<const uint32_t*>(src);
-  } else if constexpr (N == 8) {
+  } else if constexpr (N == 2) {
     const uint2 v = *reinterpret_cast<const uint2*>(src);
     dst[0] = v.x;
     dst[1] = v.y;
   } else {
 #pragma unroll
-    for (int i = 0; i < N / 16; ++i) {
+    for (int i = 0; i < N / 4; ++i) {
       const uint4 v = reinterpret_cast<const uint4*>(src)[i];
       dst[4 * i + 0] = v.x;
       dst[4 * i + 1] = v.y;
@@ -96,25 +118,91 @@ __device__ __forceinline__ void lds_bytes(uint32_t* dst, const uint8_t* src) {
   }
 }
 
-template <typename T>
-__device__ __forceinline__ float sc_to_f32(const uint8_t* p) {
-  return Elem<T>::bits_to_f32(*reinterpret_cast<const uint16_t*>(p));
+// G consecutive scale-dtype values of one key row -> float.
+template <typename T, int G>
+__device__ __forceinline__ void lds_scales(float* dst, const uint8_t* src) {
+  const uint16_t* p = reinterpret_cast<const uint16_t*>(src);
+  if constexpr (G == 1) {
+    dst[0] = Elem<T>::bits_to_f32(p[0]);
+  } else if constexpr (G == 2) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(src);
+    dst[0] = Elem<T>::bits_to_f32((uint16_t)(w & 0xffffu));
+    dst[1] = Elem<T>::bits_to_f32((uint16_t)(w >> 16));
+  } else {
+    const uint2 w = *reinterpret_cast<const uint2*>(src);
+    dst[0] = Elem<T>::bits_to_f32((uint16_t)(w.x & 0xffffu));
+    dst[1] = Elem<T>::bits_to_f32((uint16_t)(w.x >> 16));
+    dst[2] = Elem<T>::bits_to_f32((uint16_t)(w.y & 0xffffu));
+    dst[3] = Elem<T>::bits_to_f32((uint16_t)(w.y >> 16));
+  }
 }
 
-constexpr uint32_t kMagic = 0x64006400u;  // f16x2 {1024, 1024}
-
-__device__ __forceinline__ uint32_t deq2(uint32_t biased, uint32_t s2, uint32_t b2) {
-  const __half2 x = __hsub2(u32_as_h2(biased), u32_as_h2(kMagic));
-  return h2_as_u32(__hfma2(x, u32_as_h2(s2), u32_as_h2(b2)));
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
 }
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(const void* local, uint32_t cta) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(cta));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Position of output element (query row r, head dim d) in the MMA fragment order the
+// consumer warps publish their accumulators in.
+template <int G, int KS>
+__device__ __forceinline__ int frag_index(int r, int d) {
+  const int nt = r >> 3, rr = r & 7, tq = rr >> 1, ir = rr & 1;
+  const int g = d >> 6, dd = d & 63, gq = dd >> 3, d8 = dd & 7, jj = d8 >> 1, ih = d8 & 1;
+  const int j = g * KS + jj;
+  return ((nt * G * KS + j) * 32 + 4 * gq + tq) * 4 + 2 * ih + ir;
+}
+
+struct DecodeParams {
+  AttnArgs a;
+  CUtensorMap tmk;  // K codes: (RB bytes, NP, B*HKV)
+  CUtensorMap tmv;  // V codes
+  float* gpart;     // cluster partials [clusters][B*HQ*S][D+4]
+  int clusters;     // clusters per (b, kv head, row group) = splits / cluster size
+};
 
 template <typename T, int BITS, int D, int NT>
-__global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(AttnArgs a) {
-  using C = Cfg<T, BITS, D>;
+__global__ void __launch_bounds__(kThreads, (NT == 1 && D <= 128) ? 3 : 2) decode_kernel(const __grid_constant__ DecodeParams P) {
+  constexpr int kSub = sub_tiles<D, NT>();
+  constexpr int kTP = 64 * kSub;  // keys per stage
+  using GG = Geo<BITS, D, kTP>;
+  constexpr int G = GG::G;
   constexpr int RG = 8 * NT;  // query rows per CTA
-  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int KS = 4;       // k-steps (and m-tiles) per scale group
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // swizzled TMA tiles need 1024-byte aligned stage buffers: align by hand
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full_bar[4], empty_bar[4];
+  __shared__ __align__(16) T q_sh[RG * D];  // this CTA's query rows
 
+  const AttnArgs& a = P.a;
+  // Programmatic dependent launch: the next kernel in the stream may be scheduled as soon as
+  // every CTA of this one has started. Reads of anything a predecessor may still be writing
+  // wait for griddepcontrol.wait below; only the producer's first stages of cache positions
+  // below a.prefetch_limit (older than the tokens appended by the predecessor) go earlier.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int split = blockIdx.x;
   const int hkv = blockIdx.y % a.HKV;
   const int rg = blockIdx.y / a.HKV;
@@ -123,18 +211,20 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(AttnArgs a) {
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;  // MMA group id
   const int tq = lane & 3;   // thread in group
+  const uint32_t crank = cluster_rank();
+  const int csize = a.cluster;       // CTAs per cluster
+  const int cidx = split / csize;    // cluster index within the row group
 
   const int gqa = a.HQ / a.HKV;
   const int R = gqa * a.S;  // query rows sharing this kv head
-  int len = a.lens ? a.lens[b] : a.n;
-  len = min(max(len, 0), a.NP);
   const int p_begin = split * a.chunk;
-  const int p_end = min(p_begin + a.chunk, len);
-  const int n_iters = p_end > p_begin ? (p_end - p_begin + kTP - 1) / kTP : 0;
   const long long bh = (long long)b * a.HKV + hkv;
+  const long long row0 = ((long long)b * a.HQ + (long long)hkv * gqa) * a.S;  // first q row
+  const int rbase = rg * RG;
+  const int rows_here = min(RG, R - rbase);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < GG::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kWarps);
     }
@@ -142,366 +232,557 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(AttnArgs a) {
   }
   __syncthreads();
 
+  // stage issue (producer lane 0); returns false if a bounded wait ran out
+  auto issue_stage = [&](int it) {
+    const int slot = it % GG::STAGES;
+    const int p0 = p_begin + it * kTP;
+    const int rows = min(kTP, a.NP - p0);
+    const uint32_t sb = rows * G * 2;
+    uint8_t* st = smem + slot * GG::STAGE_BYTES;
+    const uint8_t* ks = (const uint8_t*)a.ks + (bh * a.NP + p0) * G * 2;
+    const uint8_t* kb = (const uint8_t*)a.kb + (bh * a.NP + p0) * G * 2;
+    const uint8_t* vs = (const uint8_t*)a.vs + (bh * a.NP + p0) * G * 2;
+    const uint8_t* vb = (const uint8_t*)a.vb + (bh * a.NP + p0) * G * 2;
+    // boxes of kBoxRows keys; boxes that start past the cache's end are not issued
+    const int boxes = (rows + kBoxRows - 1) / kBoxRows;
+    mbar_arrive_expect_tx(&full_bar[slot], 2 * GG::NBOX * boxes * kBoxRows * GG::RBOX + 4 * sb);
+#pragma unroll
+    for (int bx = 0; bx < GG::NBOX; ++bx) {
+#pragma unroll
+      for (int j = 0; j < kSub; ++j) {
+        if (j < boxes) {
+          const int off = bx * kTP * GG::RBOX + j * kBoxRows * GG::RBOX;
+          tma_load_3d(st + GG::OFF_KC + off, &P.tmk, bx * GG::RBOX, p0 + j * kBoxRows, (int)bh,
+                      &full_bar[slot]);
+          tma_load_3d(st + GG::OFF_VC + off, &P.tmv, bx * GG::RBOX, p0 + j * kBoxRows, (int)bh,
+                      &full_bar[slot]);
+        }
+      }
+    }
+    bulk_g2s(st + GG::OFF_KS, ks, sb, &full_bar[slot]);
+    bulk_g2s(st + GG::OFF_KB, kb, sb, &full_bar[slot]);
+    bulk_g2s(st + GG::OFF_VS, vs, sb, &full_bar[slot]);
+    bulk_g2s(st + GG::OFF_VB, vb, sb, &full_bar[slot]);
+  };
+  int pre = 0;  // stages issued before the dependency wait
+  if (warp == kWarps && lane == 0 && !a.lens) {
+    const int len0 = min(max(a.n, 0), a.NP);
+    const int end0 = min(p_begin + a.chunk, len0);
+    const int it0 = end0 > p_begin ? (end0 - p_begin + kTP - 1) / kTP : 0;
+    while (pre < GG::STAGES && pre < it0 && p_begin + (pre + 1) * kTP <= a.prefetch_limit)
+      issue_stage(pre++);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int len = a.lens ? a.lens[b] : a.n;
+  len = min(max(len, 0), a.NP);
+  const int p_end = min(p_begin + a.chunk, len);
+  const int n_iters = p_end > p_begin ? (p_end - p_begin + kTP - 1) / kTP : 0;
+
+  // merge area (reuses the stage ring once the main loop is over)
+  float* mw = reinterpret_cast<float*>(smem);  // [kWarps][RG] running max per warp
+  float* lw = mw + kWarps * RG;                // [kWarps][RG] sums
+  float* ow = lw + kWarps * RG;                // [kWarps][RG*D] outputs, fragment order
+  float* cp = ow + kWarps * RG * D;            // [RG*D] this CTA's output, fragment order
+  float* cm = cp + RG * D;                     // [RG] this CTA's max per row
+  float* cl = cm + RG;                         // [RG] this CTA's sum per row
+  float* tm = cl + RG;                         // [kMaxCluster][RG] cluster members' max
+  float* tl = tm + kMaxCluster * RG;           // [kMaxCluster][RG] their sums
+  float* tf = tl + kMaxCluster * RG;           // [kMaxCluster][RG] their weights
+  float* ml = tf + kMaxCluster * RG;           // [2][RG] cluster max and sum per row
+
   if (warp == kWarps) {
     // ------------------------------ producer -------------------------------------------
     if (lane == 0) {
-      const uint8_t* kw = (const uint8_t*)a.kw + bh * a.NP * C::RB;
-      const uint8_t* vw = (const uint8_t*)a.vw + bh * a.NP * C::RB;
-      const uint8_t* ks = (const uint8_t*)a.ks + bh * a.NP * C::G * 2;
-      const uint8_t* kb = (const uint8_t*)a.kb + bh * a.NP * C::G * 2;
-      const uint8_t* vs = (const uint8_t*)a.vs + bh * a.NP * C::G * 2;
-      const uint8_t* vb = (const uint8_t*)a.vb + bh * a.NP * C::G * 2;
       bool ok = true;
-      for (int it = 0; it < n_iters && ok; ++it) {
-        const int slot = it % C::STAGES;
-        if (it >= C::STAGES) ok = mbar_wait(&empty_bar[slot], ((it / C::STAGES) - 1) & 1, a.status, 1);
+      for (int it = pre; it < n_iters && ok; ++it) {
+        const int slot = it % GG::STAGES;
+        if (it >= GG::STAGES)
+          ok = mbar_wait(&empty_bar[slot], ((it / GG::STAGES) - 1) & 1, a.status, 11);
         if (!ok) break;
-        const int p0 = p_begin + it * kTP;
-        const int rows = min(kTP, a.NP - p0);
-        const uint32_t cb = rows * C::RB, sb = rows * C::G * 2;
-        uint8_t* st = smem + slot * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full_bar[slot], 2 * cb + 4 * sb);
-        bulk_g2s(st + C::OFF_KC, kw + (size_t)p0 * C::RB, cb, &full_bar[slot]);
-        bulk_g2s(st + C::OFF_VC, vw + (size_t)p0 * C::RB, cb, &full_bar[slot]);
-        bulk_g2s(st + C::OFF_KS, ks + (size_t)p0 * C::G * 2, sb, &full_bar[slot]);
-        bulk_g2s(st + C::OFF_KB, kb + (size_t)p0 * C::G * 2, sb, &full_bar[slot]);
-        bulk_g2s(st + C::OFF_VS, vs + (size_t)p0 * C::G * 2, sb, &full_bar[slot]);
-        bulk_g2s(st + C::OFF_VB, vb + (size_t)p0 * C::G * 2, sb, &full_bar[slot]);
+        issue_stage(it);
       }
-      // drain: every issued stage must land before the CTA may exit
-      const int issued = n_iters;
-      for (int it = max(0, issued - C::STAGES); it < issued; ++it)
-        mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, a.status, 2);
-    }
-    return;
-  }
-
-  // -------------------------------- consumers -------------------------------------------
-  const T* qg = (const T*)a.q;
-  const float qmul = a.scale * 1.4426950408889634f;  // softmax in base 2
-  const long long row0 = ((long long)b * a.HQ + (long long)hkv * gqa) * a.S;  // first q row
-  const int rbase = rg * RG;
-
-  // Q as the B operand of QK (k = head_dim pairs in this lane's K-code order, n = row).
-  uint32_t qf[NT][C::KS][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int r = rbase + nt * 8 + gq;
-    const bool rv = r < R;
-    const T* qr = qg + (row0 + (rv ? r : 0)) * D + tq * (D / 4);
-#pragma unroll
-    for (int k = 0; k < C::KS; ++k) {
-      int d0, d1, d2, d3;  // lo pair (d0,d1), hi pair (d2,d3), relative to this lane's quarter
-      if constexpr (BITS == 4) {
-        const int w = k >> 1, h = k & 1;
-        d0 = 8 * w + 2 * h;
-        d1 = d0 + 4;
-        d2 = d0 + 1;
-        d3 = d0 + 5;
-      } else {
-        d0 = 4 * k;
-        d1 = d0 + 2;
-        d2 = d0 + 1;
-        d3 = d0 + 3;
-      }
-      const float v0 = rv ? Elem<T>::to_f32(qr[d0]) * qmul : 0.f;
-      const float v1 = rv ? Elem<T>::to_f32(qr[d1]) * qmul : 0.f;
-      const float v2 = rv ? Elem<T>::to_f32(qr[d2]) * qmul : 0.f;
-      const float v3 = rv ? Elem<T>::to_f32(qr[d3]) * qmul : 0.f;
-      qf[nt][k][0] = pack_f16x2(v0, v1);
-      qf[nt][k][1] = pack_f16x2(v2, v3);
-    }
-  }
-
-  float o[NT][C::KS][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int j = 0; j < C::KS; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[nt][j][i] = 0.f;
-  float m_run[NT][2], l_run[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    m_run[nt][0] = m_run[nt][1] = kNegInf;
-    l_run[nt][0] = l_run[nt][1] = 0.f;
-  }
-
-  const int kg = tq * D / 256;  // scale group of this lane's K quarter
-  const int vg = gq * D / 512;  // scale group of this lane's V eighth
-  const int kr0 = key_perm<BITS>(gq), kr1 = key_perm<BITS>(gq + 8);
-  const int vr0 = key_perm<BITS>(2 * tq), vr1 = key_perm<BITS>(2 * tq + 1);
-  const int vr2 = key_perm<BITS>(2 * tq + 8), vr3 = key_perm<BITS>(2 * tq + 9);
-  const bool any_mask = a.mask_kind != QKV_MASK_NONE;
-  const int pb = a.pos_base ? a.pos_base[b] : 0;
-  const int tot = a.total_lens ? a.total_lens[b] : len;
-
-  bool ok = true;
-  for (int it = 0; it < n_iters; ++it) {
-    const int slot = it % C::STAGES;
-    ok = mbar_wait(&full_bar[slot], (it / C::STAGES) & 1, a.status, 3);
-    if (!ok) break;
-    const uint8_t* st = smem + slot * C::STAGE_BYTES;
-    const int tile0 = warp * 16;  // this warp's first key row in the stage
-    const int p0 = p_begin + it * kTP + tile0;
-    if (p0 < p_end) {
-      // ---- scores^T = K . Q^T ----------------------------------------------------------
-      float s[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      {
-        uint32_t kc0[C::KCHUNK / 4], kc1[C::KCHUNK / 4];
-        lds_bytes<C::KCHUNK>(kc0, st + C::OFF_KC + (tile0 + kr0) * C::RB + tq * C::KCHUNK);
-        lds_bytes<C::KCHUNK>(kc1, st + C::OFF_KC + (tile0 + kr1) * C::RB + tq * C::KCHUNK);
-        const float s0 = sc_to_f32<T>(st + C::OFF_KS + ((tile0 + kr0) * C::G + kg) * 2);
-        const float s1 = sc_to_f32<T>(st + C::OFF_KS + ((tile0 + kr1) * C::G + kg) * 2);
-        const float b0 = sc_to_f32<T>(st + C::OFF_KB + ((tile0 + kr0) * C::G + kg) * 2);
-        const float b1 = sc_to_f32<T>(st + C::OFF_KB + ((tile0 + kr1) * C::G + kg) * 2);
-        const uint32_t s20 = pack_f16x2(s0, s0), s21 = pack_f16x2(s1, s1);
-        const uint32_t b20 = pack_f16x2(b0, b0), b21 = pack_f16x2(b1, b1);
-        if constexpr (BITS == 4) {
-          const uint32_t t20 = pack_f16x2(s0 * 0.0625f, s0 * 0.0625f);
-          const uint32_t t21 = pack_f16x2(s1 * 0.0625f, s1 * 0.0625f);
-#pragma unroll
-          for (int w = 0; w < C::KCHUNK / 4; ++w) {
-            const uint32_t x0 = kc0[w], x1 = kc1[w];
-            const uint32_t y0 = x0 >> 8, y1 = x1 >> 8;
-            uint32_t af[4];
-            af[0] = deq2(and_or(x0, 0x000F000Fu, kMagic), s20, b20);
-            af[1] = deq2(and_or(x1, 0x000F000Fu, kMagic), s21, b21);
-            af[2] = deq2(and_or(x0, 0x00F000F0u, kMagic), t20, b20);
-            af[3] = deq2(and_or(x1, 0x00F000F0u, kMagic), t21, b21);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(s[nt], af, qf[nt][2 * w][0], qf[nt][2 * w][1]);
-            af[0] = deq2(and_or(y0, 0x000F000Fu, kMagic), s20, b20);
-            af[1] = deq2(and_or(y1, 0x000F000Fu, kMagic), s21, b21);
-            af[2] = deq2(and_or(y0, 0x00F000F0u, kMagic), t20, b20);
-            af[3] = deq2(and_or(y1, 0x00F000F0u, kMagic), t21, b21);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              mma16816(s[nt], af, qf[nt][2 * w + 1][0], qf[nt][2 * w + 1][1]);
-          }
-        } else {
-#pragma unroll
-          for (int w = 0; w < C::KCHUNK / 4; ++w) {
-            const uint32_t x0 = kc0[w], x1 = kc1[w];
-            uint32_t af[4];
-            af[0] = deq2(prmt(x0, kMagic, 0x5250), s20, b20);
-            af[1] = deq2(prmt(x1, kMagic, 0x5250), s21, b21);
-            af[2] = deq2(prmt(x0, kMagic, 0x5351), s20, b20);
-            af[3] = deq2(prmt(x1, kMagic, 0x5351), s21, b21);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(s[nt], af, qf[nt][w][0], qf[nt][w][1]);
-          }
-        }
-      }
-
-      // ---- masking (only tiles that need it) -------------------------------------------
-      if (p0 + 16 > p_end || any_mask) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int key = p0 + ((i < 2) ? kr0 : kr1);
-            const int r = rbase + nt * 8 + 2 * tq + (i & 1);
-            bool keep = key < p_end;
-            float add = 0.f;
-            if (keep && any_mask && r < R) {
-              const int sq = r % a.S;
-              if (a.mask_kind == QKV_MASK_CAUSAL) {
-                keep = pb + key <= tot - a.S + sq;
-              } else {
-                const int hq = hkv * gqa + r / a.S;
-                const long long off = (long long)b * a.mask_sb + (long long)hq * a.mask_sh +
-                                      (long long)sq * a.mask_sq + key;
-                if (key >= a.mask_nk) {
-                  keep = false;
-                } else if (a.mask_kind == QKV_MASK_BOOL) {
-                  keep = ((const uint8_t*)a.mask)[off] != 0;
-                } else {
-                  add = Elem<T>::to_f32(((const T*)a.mask)[off]) * 1.4426950408889634f;
-                }
-              }
-            }
-            s[nt][i] = keep ? s[nt][i] + add : kNegInf;
-          }
-      }
-
-      // ---- online softmax (base 2) -----------------------------------------------------
-      uint32_t pf[NT][2];
-      bool rescale = false;
-      float fac[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float p[4];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float mt = fmaxf(s[nt][c], s[nt][2 + c]);
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-          const float m_new = fmaxf(m_run[nt][c], mt);
-          const float m_use = m_new == kNegInf ? 0.f : m_new;
-          fac[nt][c] = ex2(m_run[nt][c] - m_use);
-          rescale |= m_new != m_run[nt][c];
-          p[c] = ex2(s[nt][c] - m_use);
-          p[2 + c] = ex2(s[nt][2 + c] - m_use);
-          l_run[nt][c] = l_run[nt][c] * fac[nt][c] + (p[c] + p[2 + c]);
-          m_run[nt][c] = m_new;
-        }
-        pf[nt][0] = movmatrix_trans(pack_f16x2(p[0], p[1]));
-        pf[nt][1] = movmatrix_trans(pack_f16x2(p[2], p[3]));
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int j = 0; j < C::KS; ++j) {
-            o[nt][j][0] *= fac[nt][0];
-            o[nt][j][1] *= fac[nt][1];
-            o[nt][j][2] *= fac[nt][0];
-            o[nt][j][3] *= fac[nt][1];
-          }
-      }
-
-      // ---- out^T += V^T . P^T ------------------------------------------------------------
-      {
-        uint32_t v0[C::VCHUNK / 4], v1[C::VCHUNK / 4], v2[C::VCHUNK / 4], v3[C::VCHUNK / 4];
-        const uint8_t* vc = st + C::OFF_VC + gq * C::VCHUNK;
-        lds_bytes<C::VCHUNK>(v0, vc + (tile0 + vr0) * C::RB);
-        lds_bytes<C::VCHUNK>(v1, vc + (tile0 + vr1) * C::RB);
-        lds_bytes<C::VCHUNK>(v2, vc + (tile0 + vr2) * C::RB);
-        lds_bytes<C::VCHUNK>(v3, vc + (tile0 + vr3) * C::RB);
-        const uint8_t* vsp = st + C::OFF_VS + vg * 2;
-        const uint8_t* vbp = st + C::OFF_VB + vg * 2;
-        float sv[4], bv[4];
-        sv[0] = sc_to_f32<T>(vsp + (tile0 + vr0) * C::G * 2);
-        sv[1] = sc_to_f32<T>(vsp + (tile0 + vr1) * C::G * 2);
-        sv[2] = sc_to_f32<T>(vsp + (tile0 + vr2) * C::G * 2);
-        sv[3] = sc_to_f32<T>(vsp + (tile0 + vr3) * C::G * 2);
-        bv[0] = sc_to_f32<T>(vbp + (tile0 + vr0) * C::G * 2);
-        bv[1] = sc_to_f32<T>(vbp + (tile0 + vr1) * C::G * 2);
-        bv[2] = sc_to_f32<T>(vbp + (tile0 + vr2) * C::G * 2);
-        bv[3] = sc_to_f32<T>(vbp + (tile0 + vr3) * C::G * 2);
-        if (p0 + 16 > p_end) {
-          // keys past the valid range carry weight 0 but their codes/scales may be
-          // anything (padded tail); force finite values so 0 * V stays 0
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int kk = (i == 0) ? vr0 : (i == 1) ? vr1 : (i == 2) ? vr2 : vr3;
-            if (p0 + kk >= p_end) sv[i] = bv[i] = 0.f;
-          }
-        }
-        const uint32_t s01 = pack_f16x2(sv[0], sv[1]), s23 = pack_f16x2(sv[2], sv[3]);
-        const uint32_t b01 = pack_f16x2(bv[0], bv[1]), b23 = pack_f16x2(bv[2], bv[3]);
-        if constexpr (BITS == 4) {
-          const uint32_t t01 = pack_f16x2(sv[0] * 0.0625f, sv[1] * 0.0625f);
-          const uint32_t t23 = pack_f16x2(sv[2] * 0.0625f, sv[3] * 0.0625f);
-#pragma unroll
-          for (int u = 0; u < C::VCHUNK / 4; ++u) {
-            const uint32_t xa = prmt(v0[u], v1[u], 0x5410), ya = prmt(v0[u], v1[u], 0x7632);
-            const uint32_t xb = prmt(v2[u], v3[u], 0x5410), yb = prmt(v2[u], v3[u], 0x7632);
-            const uint32_t srcA[4] = {xa, xa >> 8, ya, ya >> 8};
-            const uint32_t srcB[4] = {xb, xb >> 8, yb, yb >> 8};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t af[4];
-              af[0] = deq2(and_or(srcA[i], 0x000F000Fu, kMagic), s01, b01);
-              af[1] = deq2(and_or(srcA[i], 0x00F000F0u, kMagic), t01, b01);
-              af[2] = deq2(and_or(srcB[i], 0x000F000Fu, kMagic), s23, b23);
-              af[3] = deq2(and_or(srcB[i], 0x00F000F0u, kMagic), t23, b23);
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) mma16816(o[nt][4 * u + i], af, pf[nt][0], pf[nt][1]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < C::VCHUNK / 4; ++u) {
-            const uint32_t xa = prmt(v0[u], v1[u], 0x5140), ya = prmt(v0[u], v1[u], 0x7362);
-            const uint32_t xb = prmt(v2[u], v3[u], 0x5140), yb = prmt(v2[u], v3[u], 0x7362);
-            uint32_t af[4];
-            af[0] = deq2(prmt(xa, kMagic, 0x5150), s01, b01);
-            af[1] = deq2(prmt(xa, kMagic, 0x5352), s01, b01);
-            af[2] = deq2(prmt(xb, kMagic, 0x5150), s23, b23);
-            af[3] = deq2(prmt(xb, kMagic, 0x5352), s23, b23);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(o[nt][2 * u], af, pf[nt][0], pf[nt][1]);
-            af[0] = deq2(prmt(ya, kMagic, 0x5150), s01, b01);
-            af[1] = deq2(prmt(ya, kMagic, 0x5352), s01, b01);
-            af[2] = deq2(prmt(yb, kMagic, 0x5150), s23, b23);
-            af[3] = deq2(prmt(yb, kMagic, 0x5352), s23, b23);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) mma16816(o[nt][2 * u + 1], af, pf[nt][0], pf[nt][1]);
-          }
-        }
-      }
+      // every issued stage lands before the ring is reused for the merge
+      for (int it = max(0, n_iters - GG::STAGES); it < n_iters; ++it)
+        mbar_wait(&full_bar[it % GG::STAGES], (it / GG::STAGES) & 1, a.status, 12);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[slot]);
-  }
-
-  // ---- merge the four warps' partials and write this CTA's partial -------------------
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float l = l_run[nt][c];
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      l_run[nt][c] = l;
+  } else {
+    // -------------------------------- consumers -----------------------------------------
+    const T* qg = (const T*)a.q;
+    const float qmul = a.scale * 1.4426950408889634f;  // softmax in base 2
+    {
+      // the CTA's RG query rows (contiguous in q) into shared memory, 16 bytes per lane
+      constexpr int V16 = RG * D * (int)sizeof(T) / 16;
+      const uint4* src = reinterpret_cast<const uint4*>(qg + (row0 + rbase) * D);
+      uint4* dst = reinterpret_cast<uint4*>(q_sh);
+      const int valid16 = rows_here * D * (int)sizeof(T) / 16;
+      for (int k = threadIdx.x; k < V16; k += kWarps * 32)
+        dst[k] = k < valid16 ? src[k] : make_uint4(0u, 0u, 0u, 0u);
+      named_bar_sync(1, kWarps * 32);
     }
-  named_bar_sync(1, kWarps * 32);  // every consumer is done with the stage ring
-  float* mw = reinterpret_cast<float*>(smem);      // [kWarps][RG]
-  float* lw = mw + kWarps * RG;                    // [kWarps][RG]
-  float* ow = lw + kWarps * RG;                    // [kWarps][RG][D]
-  if (gq == 0) {
+
+    // Q as the B operand of QK, per scale group: k = head_dim pairs in this lane's code
+    // order (the 4-bit "x16" slots pre-divided by 16), n = query row. The group sums of the
+    // same f16 values feed the bias term.
+    uint32_t qf[NT][G][KS][2];
+    float qsum_mine[NT][G];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int r = rbase + nt * 8 + gq;
+      const bool rv = r < R;
+      const T* qr = q_sh + (nt * 8 + gq) * D;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float acc = 0.f;
+        const int base = 64 * g + 16 * tq;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          int d0, d1, d2, d3;
+          if constexpr (BITS == 4) {
+            const int u = k >> 1, h = k & 1;
+            d0 = 8 * u + 2 * h;
+            d1 = d0 + 4;
+            d2 = d0 + 1;
+            d3 = d0 + 5;
+          } else {
+            d0 = 4 * k;
+            d1 = d0 + 2;
+            d2 = d0 + 1;
+            d3 = d0 + 3;
+          }
+          const float v0 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d0]) * qmul)) : 0.f;
+          const float v1 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d1]) * qmul)) : 0.f;
+          const float v2 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d2]) * qmul)) : 0.f;
+          const float v3 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d3]) * qmul)) : 0.f;
+          acc += (v0 + v1) + (v2 + v3);
+          const float hs = BITS == 4 ? 0.0625f : 1.f;
+          qf[nt][g][k][0] = pack_f16x2(v0, v1);
+          qf[nt][g][k][1] = pack_f16x2(v2 * hs, v3 * hs);
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        qsum_mine[nt][g] = acc;  // for row nt*8 + gq
+      }
+    }
+    // this lane's score columns are rows 2*tq, 2*tq+1 of each n-tile
+    float qsum[NT][2][G];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        qsum[nt][0][g] = __shfl_sync(0xffffffffu, qsum_mine[nt][g], 8 * tq);
+        qsum[nt][1][g] = __shfl_sync(0xffffffffu, qsum_mine[nt][g], 8 * tq + 4);
+      }
+
+    float o[NT][G * KS][4];
+    float obias[NT][2][G];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < G * KS; ++j) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int g = 0; g < G; ++g) obias[nt][c][g] = 0.f;
+    }
+    float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = kNegInf;
+      l_run[nt][0] = l_run[nt][1] = 0.f;
+    }
+
+    const int kA = key_perm<BITS>(gq), kB = key_perm<BITS>(gq + 8);
+    const int v0k = key_perm<BITS>(2 * tq), v1k = key_perm<BITS>(2 * tq + 1);
+    const int v2k = key_perm<BITS>(2 * tq + 8), v3k = key_perm<BITS>(2 * tq + 9);
+    const bool any_mask = a.mask_kind != QKV_MASK_NONE;
+    const int pb = a.pos_base ? a.pos_base[b] : 0;
+    const int tot = a.total_lens ? a.total_lens[b] : len;
+
+    // Each warp owns 2 x 16 consecutive keys of every stage. The two sub-tiles run their
+    // products as independent MMA chains and share one softmax max-reduction.
+    for (int it = 0; it < n_iters; ++it) {
+      const int slot = it % GG::STAGES;
+      if (!mbar_wait(&full_bar[slot], (it / GG::STAGES) & 1, a.status, 13)) break;
+      const uint8_t* st = smem + slot * GG::STAGE_BYTES;
+      const int t0 = warp * (16 * kSub);  // this warp's first key row in the stage
+      const int p0 = p_begin + it * kTP + t0;
+      if (p0 < p_end) {
+        const bool tail = p0 + 16 * kSub > p_end;
+        // ---- scores^T = codes(K) . Q^T per scale group, both sub-tiles ------------------
+        float acc[kSub][NT][G][4];
+#pragma unroll
+        for (int h = 0; h < kSub; ++h)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+              acc[h][nt][g][0] = acc[h][nt][g][1] = acc[h][nt][g][2] = acc[h][nt][g][3] = 0.f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int h = 0; h < kSub; ++h) {
+            uint32_t wa[GG::KW], wb[GG::KW];
+            lds_words<GG::KW>(wa, st + GG::OFF_KC + code_off<BITS, D, kTP>(t0 + 16 * h + kA, g * GG::GB + tq * GG::KLB));
+            lds_words<GG::KW>(wb, st + GG::OFF_KC + code_off<BITS, D, kTP>(t0 + 16 * h + kB, g * GG::GB + tq * GG::KLB));
+            if constexpr (BITS == 4) {
+#pragma unroll
+              for (int u = 0; u < GG::KW; ++u) {
+                const uint32_t ya = wa[u] >> 8, yb = wb[u] >> 8;
+                uint32_t af[4];
+                af[0] = wa[u] & 0x000F000Fu;
+                af[1] = wb[u] & 0x000F000Fu;
+                af[2] = wa[u] & 0x00F000F0u;
+                af[3] = wb[u] & 0x00F000F0u;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  mma16816(acc[h][nt][g], af, qf[nt][g][2 * u][0], qf[nt][g][2 * u][1]);
+                af[0] = ya & 0x000F000Fu;
+                af[1] = yb & 0x000F000Fu;
+                af[2] = ya & 0x00F000F0u;
+                af[3] = yb & 0x00F000F0u;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  mma16816(acc[h][nt][g], af, qf[nt][g][2 * u + 1][0], qf[nt][g][2 * u + 1][1]);
+              }
+            } else {
+#pragma unroll
+              for (int u = 0; u < GG::KW; ++u) {
+                uint32_t af[4];
+                af[0] = prmt(wa[u], 0u, 0x4240);
+                af[1] = prmt(wb[u], 0u, 0x4240);
+                af[2] = prmt(wa[u], 0u, 0x4341);
+                af[3] = prmt(wb[u], 0u, 0x4341);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) mma16816(acc[h][nt][g], af, qf[nt][g][u][0], qf[nt][g][u][1]);
+              }
+            }
+          }
+        }
+        float s[kSub][NT][4];
+#pragma unroll
+        for (int h = 0; h < kSub; ++h) {
+          float ksA[G], kbA[G], ksB[G], kbB[G];
+          lds_scales<T, G>(ksA, st + GG::OFF_KS + (t0 + 16 * h + kA) * G * 2);
+          lds_scales<T, G>(ksB, st + GG::OFF_KS + (t0 + 16 * h + kB) * G * 2);
+          lds_scales<T, G>(kbA, st + GG::OFF_KB + (t0 + 16 * h + kA) * G * 2);
+          lds_scales<T, G>(kbB, st + GG::OFF_KB + (t0 + 16 * h + kB) * G * 2);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float v = 0.f;
+#pragma unroll
+              for (int g = 0; g < G; ++g) {
+                const float sc = (i < 2 ? ksA[g] : ksB[g]) * 16777216.0f;
+                const float bi = i < 2 ? kbA[g] : kbB[g];
+                v = fmaf(sc, acc[h][nt][g][i], fmaf(bi, qsum[nt][i & 1][g], v));
+              }
+              s[h][nt][i] = v;
+            }
+        }
+
+        // ---- masking (only tiles that need it) ----------------------------------------
+        if (tail || any_mask) {
+#pragma unroll
+          for (int h = 0; h < kSub; ++h)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int key = p0 + 16 * h + ((i < 2) ? kA : kB);
+                const int r = rbase + nt * 8 + 2 * tq + (i & 1);
+                bool keep = key < p_end;
+                float add = 0.f;
+                if (keep && any_mask && r < R) {
+                  const int sq = r % a.S;
+                  if (a.mask_kind == QKV_MASK_CAUSAL) {
+                    keep = pb + key <= tot - a.S + sq;
+                  } else {
+                    const int hq = hkv * gqa + r / a.S;
+                    const long long off = (long long)b * a.mask_sb + (long long)hq * a.mask_sh +
+                                          (long long)sq * a.mask_sq + key;
+                    if (key >= a.mask_nk) {
+                      keep = false;
+                    } else if (a.mask_kind == QKV_MASK_BOOL) {
+                      keep = ((const uint8_t*)a.mask)[off] != 0;
+                    } else {
+                      add = Elem<T>::to_f32(((const T*)a.mask)[off]) * 1.4426950408889634f;
+                    }
+                  }
+                }
+                s[h][nt][i] = keep ? s[h][nt][i] + add : kNegInf;
+              }
+        }
+
+        // ---- online softmax (base 2), one max-reduction for both sub-tiles ---------------
+        float vsA[kSub][G], vbA[kSub][G], vsB[kSub][G], vbB[kSub][G];
+#pragma unroll
+        for (int h = 0; h < kSub; ++h) {
+          lds_scales<T, G>(vsA[h], st + GG::OFF_VS + (t0 + 16 * h + kA) * G * 2);
+          lds_scales<T, G>(vsB[h], st + GG::OFF_VS + (t0 + 16 * h + kB) * G * 2);
+          lds_scales<T, G>(vbA[h], st + GG::OFF_VB + (t0 + 16 * h + kA) * G * 2);
+          lds_scales<T, G>(vbB[h], st + GG::OFF_VB + (t0 + 16 * h + kB) * G * 2);
+          if (tail) {
+            // keys past the valid range carry weight 0; their scales may be anything
+            // (padded tail), so zero them to keep 0 * V finite
+            if (p0 + 16 * h + kA >= p_end) {
+#pragma unroll
+              for (int g = 0; g < G; ++g) vsA[h][g] = vbA[h][g] = 0.f;
+            }
+            if (p0 + 16 * h + kB >= p_end) {
+#pragma unroll
+              for (int g = 0; g < G; ++g) vsB[h][g] = vbB[h][g] = 0.f;
+            }
+          }
+        }
+        uint32_t pf[kSub][NT][G][2];
+        bool rescale = false;
+        float fac[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float p[kSub][4];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float mt = fmaxf(s[0][nt][c], s[0][nt][2 + c]);
+#pragma unroll
+            for (int h = 1; h < kSub; ++h) mt = fmaxf(mt, fmaxf(s[h][nt][c], s[h][nt][2 + c]));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+            const float m_new = fmaxf(m_run[nt][c], mt);
+            const float m_use = m_new == kNegInf ? 0.f : m_new;
+            fac[nt][c] = ex2(m_run[nt][c] - m_use);
+            rescale |= m_new != m_run[nt][c];
+            float lsum = 0.f;
+            float ob[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) ob[g] = obias[nt][c][g] * fac[nt][c];
+#pragma unroll
+            for (int h = 0; h < kSub; ++h) {
+              p[h][c] = ex2(s[h][nt][c] - m_use);
+              p[h][2 + c] = ex2(s[h][nt][2 + c] - m_use);
+              lsum += p[h][c] + p[h][2 + c];
+#pragma unroll
+              for (int g = 0; g < G; ++g) ob[g] = fmaf(p[h][c], vbA[h][g], fmaf(p[h][2 + c], vbB[h][g], ob[g]));
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) obias[nt][c][g] = ob[g];
+            l_run[nt][c] = fmaf(l_run[nt][c], fac[nt][c], lsum);
+            m_run[nt][c] = m_new;
+          }
+#pragma unroll
+          for (int h = 0; h < kSub; ++h)
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              pf[h][nt][g][0] = movmatrix_trans(pack_f16x2(p[h][0] * vsA[h][g], p[h][1] * vsA[h][g]));
+              pf[h][nt][g][1] = movmatrix_trans(pack_f16x2(p[h][2] * vsB[h][g], p[h][3] * vsB[h][g]));
+            }
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < G * KS; ++j) {
+              o[nt][j][0] *= fac[nt][0];
+              o[nt][j][1] *= fac[nt][1];
+              o[nt][j][2] *= fac[nt][0];
+              o[nt][j][3] *= fac[nt][1];
+            }
+        }
+
+        // ---- out^T += codes(V)^T . (P*scale)^T per scale group, both sub-tiles -----------
+#pragma unroll
+        for (int h = 0; h < kSub; ++h) {
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            uint32_t w0[GG::VW], w1[GG::VW], w2[GG::VW], w3[GG::VW];
+            const int vb0 = g * GG::GB + gq * GG::VLB;
+            const int tr = t0 + 16 * h;
+            lds_words<GG::VW>(w0, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v0k, vb0));
+            lds_words<GG::VW>(w1, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v1k, vb0));
+            lds_words<GG::VW>(w2, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v2k, vb0));
+            lds_words<GG::VW>(w3, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v3k, vb0));
+            if constexpr (BITS == 4) {
+              const uint32_t xa = prmt(w0[0], w1[0], 0x5410), ya = prmt(w0[0], w1[0], 0x7632);
+              const uint32_t xb = prmt(w2[0], w3[0], 0x5410), yb = prmt(w2[0], w3[0], 0x7632);
+              const uint32_t srcA[4] = {xa, xa >> 8, ya, ya >> 8};
+              const uint32_t srcB[4] = {xb, xb >> 8, yb, yb >> 8};
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                uint32_t af[4];
+                af[0] = srcA[jj] & 0x000F000Fu;
+                af[1] = srcA[jj] & 0x00F000F0u;
+                af[2] = srcB[jj] & 0x000F000Fu;
+                af[3] = srcB[jj] & 0x00F000F0u;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  mma16816(o[nt][g * KS + jj], af, pf[h][nt][g][0], pf[h][nt][g][1]);
+              }
+            } else {
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const uint32_t xa = prmt(w0[u], w1[u], 0x5140), ya = prmt(w0[u], w1[u], 0x7362);
+                const uint32_t xb = prmt(w2[u], w3[u], 0x5140), yb = prmt(w2[u], w3[u], 0x7362);
+                uint32_t af[4];
+                af[0] = prmt(xa, 0u, 0x4140);
+                af[1] = prmt(xa, 0u, 0x4342);
+                af[2] = prmt(xb, 0u, 0x4140);
+                af[3] = prmt(xb, 0u, 0x4342);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  mma16816(o[nt][g * KS + 2 * u], af, pf[h][nt][g][0], pf[h][nt][g][1]);
+                af[0] = prmt(ya, 0u, 0x4140);
+                af[1] = prmt(ya, 0u, 0x4342);
+                af[2] = prmt(yb, 0u, 0x4140);
+                af[3] = prmt(yb, 0u, 0x4342);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  mma16816(o[nt][g * KS + 2 * u + 1], af, pf[h][nt][g][0], pf[h][nt][g][1]);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    }
+
+    // ---- per-warp finalisation: reduce l and the bias sums over the key lanes -----------
+    float l_fin[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        mw[warp * RG + nt * 8 + 2 * tq + c] = m_run[nt][c];
-        lw[warp * RG + nt * 8 + 2 * tq + c] = l_run[nt][c];
+        float l = l_run[nt][c];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_fin[nt][c] = l;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float v = obias[nt][c][g];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          obias[nt][c][g] = v;
+        }
       }
-  }
+    named_bar_sync(1, kWarps * 32);  // every consumer is done with the stage ring
+    if (gq == 0) {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int j = 0; j < C::KS; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = nt * 8 + 2 * tq + (i & 1);
-        const int d = gq * (D / 8) + 2 * j + (i >> 1);
-        ow[(warp * RG + r) * D + d] = o[nt][j][i];
-      }
-  named_bar_sync(1, kWarps * 32);
-
-  const int rows_here = min(RG, R - rbase);
-  float* part = (float*)a.workspace + ((size_t)split * a.B * a.HQ * a.S + row0 + rbase) * (D + 4);
-  for (int idx = threadIdx.x; idx < rows_here * (D + 4); idx += kWarps * 32) {
-    const int r = idx / (D + 4), d = idx - r * (D + 4);
-    float mx = kNegInf;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, mw[w * RG + r]);
-    const float mu = mx == kNegInf ? 0.f : mx;
-    float acc = 0.f;
-    if (d < D) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) acc += ex2(mw[w * RG + r] - mu) * ow[(w * RG + r) * D + d];
-    } else if (d == D) {
-      acc = mx;
-    } else if (d == D + 1) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) acc += ex2(mw[w * RG + r] - mu) * lw[w * RG + r];
+        for (int c = 0; c < 2; ++c) mw[warp * RG + nt * 8 + 2 * tq + c] = m_run[nt][c];
     }
-    part[(size_t)r * (D + 4) + d] = acc;
+    named_bar_sync(1, kWarps * 32);
+    // rescale this warp's rows to the CTA-wide max, then publish the rows in MMA fragment
+    // order (one 16-byte store per lane per m-tile: conflict-free)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float f[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int r = nt * 8 + 2 * tq + c;
+        float mx = mw[r];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, mw[w * RG + r]);
+        f[c] = ex2(m_run[nt][c] - (mx == kNegInf ? 0.f : mx));
+        if (gq == 0) lw[warp * RG + r] = l_fin[nt][c] * f[c];
+      }
+#pragma unroll
+      for (int j = 0; j < G * KS; ++j) {
+        const int g = j / KS;
+        float4 v;
+        const float shi = BITS == 4 ? 1048576.0f : 16777216.0f;  // 2^24 (/16 for x16 rows)
+        v.x = f[0] * fmaf(o[nt][j][0], 16777216.0f, obias[nt][0][g]);
+        v.y = f[1] * fmaf(o[nt][j][1], 16777216.0f, obias[nt][1][g]);
+        v.z = f[0] * fmaf(o[nt][j][2], shi, obias[nt][0][g]);
+        v.w = f[1] * fmaf(o[nt][j][3], shi, obias[nt][1][g]);
+        reinterpret_cast<float4*>(ow + warp * RG * D)[(nt * G * KS + j) * 32 + lane] = v;
+      }
+    }
+    named_bar_sync(1, kWarps * 32);
+    float4* co4 = reinterpret_cast<float4*>(cp);
+    for (int k = threadIdx.x; k < RG * D / 4; k += kWarps * 32) {
+      float4 acc4 = reinterpret_cast<const float4*>(ow)[k];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) {
+        const float4 x = reinterpret_cast<const float4*>(ow + w * RG * D)[k];
+        acc4.x += x.x;
+        acc4.y += x.y;
+        acc4.z += x.z;
+        acc4.w += x.w;
+      }
+      co4[k] = acc4;
+    }
+    if (threadIdx.x < RG) {
+      const int r = threadIdx.x;
+      float mx = mw[r], l = lw[r];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) {
+        mx = fmaxf(mx, mw[w * RG + r]);
+        l += lw[w * RG + r];
+      }
+      cm[r] = mx;
+      cl[r] = l;
+    }
   }
+  __syncthreads();
+
+  // ---- cluster merge through distributed shared memory -> one partial per cluster --------
+  const size_t rows_all = (size_t)a.B * a.HQ * a.S;
+  float* gpart = P.gpart;  // [clusters][rows_all][D+4]
+  cluster_sync_all();
+  {
+    for (int k = threadIdx.x; k < csize * RG; k += kThreads) {
+      const int c = k / RG, r = k - c * RG;
+      tm[k] = ld_dsmem_f32(cm + r, c);
+      tl[k] = ld_dsmem_f32(cl + r, c);
+    }
+    __syncthreads();
+    if (threadIdx.x < RG) {
+      const int r = threadIdx.x;
+      float mx = kNegInf;
+      for (int c = 0; c < csize; ++c) mx = fmaxf(mx, tm[c * RG + r]);
+      const float mu = mx == kNegInf ? 0.f : mx;
+      float l = 0.f;
+      for (int c = 0; c < csize; ++c) {
+        const float f = ex2(tm[c * RG + r] - mu);
+        tf[c * RG + r] = f;
+        l += f * tl[c * RG + r];
+      }
+      ml[r] = mx;
+      ml[RG + r] = l;
+    }
+    __syncthreads();
+    const int n_el = rows_here * D;
+    for (int e = (int)crank * kThreads + threadIdx.x; e < n_el; e += csize * kThreads) {
+      const int r = e / D, d = e - r * D;
+      const int fe = frag_index<G, KS>(r, d);
+      float v = 0.f;
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c)
+        if (c < csize) v = fmaf(tf[c * RG + r], ld_dsmem_f32(cp + fe, c), v);
+      gpart[((size_t)cidx * rows_all + row0 + rbase + r) * (D + 4) + d] = v;
+    }
+    if (crank == 0 && threadIdx.x < rows_here) {
+      const int r = threadIdx.x;
+      float* dst = gpart + ((size_t)cidx * rows_all + row0 + rbase + r) * (D + 4);
+      dst[D] = ml[r];
+      dst[D + 1] = ml[RG + r];
+    }
+  }
+  cluster_sync_all();  // every remote read of this CTA's shared memory is done
+
 }
 
-// One CTA (8 warps) per output row. The split maxima are reduced by all threads at once;
-// then warp w folds splits w, w+8, ... with its lanes owning D/32 columns, and the eight
-// warp sums meet in shared memory. Independent loads keep many L2 requests in flight.
+// One CTA (8 warps) per output row. Warp w owns partials w, w+8, ... (up to kCombineBatch
+// per warp per pass): their (max, sum) and this lane's D/32 columns load in one round of
+// independent requests, then the CTA agrees on the max through shared memory and folds.
+// Rows with more than 8 * kCombineBatch partials take several passes merged online.
 constexpr int kCombineWarps = 8;
+constexpr int kCombineBatch = 8;
 
 template <typename TO, int D>
 __global__ void __launch_bounds__(kCombineWarps * 32)
@@ -510,47 +791,67 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
   constexpr int E = D / 32;
   __shared__ float red[kCombineWarps][D];
   __shared__ float wmax[kCombineWarps], wsum[kCombineWarps];
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the partials come from the kernel before
   const long long row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* base = parts + row * (D + 4);
   const size_t pstride = (size_t)part_stride_rows * (D + 4);
 
-  float mx = kNegInf;
-  for (int p = threadIdx.x; p < n_parts; p += blockDim.x) mx = fmaxf(mx, base[p * pstride + D]);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) wmax[warp] = mx;
-  __syncthreads();
-  mx = wmax[0];
-#pragma unroll
-  for (int w = 1; w < kCombineWarps; ++w) mx = fmaxf(mx, wmax[w]);
-  const float mu = mx == kNegInf ? 0.f : mx;
-
-  float l = 0.f;
-  for (int p = threadIdx.x; p < n_parts; p += blockDim.x) {
-    const float* pr = base + p * pstride;
-    l += ex2(pr[D] - mu) * pr[D + 1];
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-  if (lane == 0) wsum[warp] = l;
-
+  float run_m = kNegInf, run_l = 0.f;  // CTA-wide running state (identical in all threads)
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
-#pragma unroll 4
-  for (int p = warp; p < n_parts; p += kCombineWarps) {
-    const float* pr = base + p * pstride;
-    const float f = ex2(pr[D] - mu);
+  for (int p0 = 0; p0 < n_parts; p0 += kCombineWarps * kCombineBatch) {
+    float pm[kCombineBatch], pl[kCombineBatch], po[kCombineBatch][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] += f * pr[lane * E + e];
+    for (int k = 0; k < kCombineBatch; ++k) {
+      const int p = p0 + warp + k * kCombineWarps;
+      if (p < n_parts) {
+        const float* pr = base + p * pstride;
+        pm[k] = __ldcg(pr + D);
+        pl[k] = __ldcg(pr + D + 1);
+#pragma unroll
+        for (int e = 0; e < E; ++e) po[k][e] = __ldcg(pr + lane * E + e);
+      } else {
+        pm[k] = kNegInf;
+        pl[k] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) po[k][e] = 0.f;
+      }
+    }
+    float mx = pm[0];
+#pragma unroll
+    for (int k = 1; k < kCombineBatch; ++k) mx = fmaxf(mx, pm[k]);
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();
+    float bm = run_m;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) bm = fmaxf(bm, wmax[w]);
+    const float mu = bm == kNegInf ? 0.f : bm;
+    const float fr = ex2(run_m - mu);  // rescale what earlier passes accumulated
+    float l = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] *= fr;
+#pragma unroll
+    for (int k = 0; k < kCombineBatch; ++k) {
+      const float f = ex2(pm[k] - mu);
+      l = fmaf(f, pl[k], l);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(f, po[k][e], acc[e]);
+    }
+    if (lane == 0) wsum[warp] = l;
+    __syncthreads();
+    float tl = run_l * fr;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) tl += wsum[w];
+    run_l = tl;
+    run_m = bm;
+    __syncthreads();  // wmax/wsum are rewritten by the next pass
   }
 #pragma unroll
   for (int e = 0; e < E; ++e) red[warp][lane * E + e] = acc[e];
   __syncthreads();
-  l = 0.f;
-#pragma unroll
-  for (int w = 0; w < kCombineWarps; ++w) l += wsum[w];
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float v = 0.f;
 #pragma unroll
@@ -558,28 +859,79 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
     if (out_part) {
       out_part[row * (D + 4) + d] = v;
     } else {
-      out[row * D + d] = Elem<TO>::from_f32(l == 0.f ? v : v / l);
+      out[row * D + d] = Elem<TO>::from_f32(run_l == 0.f ? v : v / run_l);
     }
   }
   if (out_part && threadIdx.x == 0) {
     float* dst = out_part + row * (D + 4);
-    dst[D] = mx;
-    dst[D + 1] = l;
+    dst[D] = run_m;
+    dst[D + 1] = run_l;
     dst[D + 2] = 0.f;
     dst[D + 3] = 0.f;
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// host side: tensor maps, launch
+// ---------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// K or V code tensor viewed as bytes (RB, NP, B*H); box (RBOX, 64 keys, 1), swizzled.
+template <int BITS, int D>
+bool make_code_map(CUtensorMap* m, const void* base, int NP, long long bhs) {
+  using GG = Geo<BITS, D, kBoxRows>;
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)GG::RB, (cuuint64_t)NP, (cuuint64_t)bhs};
+  const cuuint64_t strides[2] = {(cuuint64_t)GG::RB, (cuuint64_t)GG::RB * (cuuint64_t)NP};
+  const cuuint32_t box[3] = {(cuuint32_t)GG::RBOX, (cuuint32_t)kBoxRows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = GG::RBOX == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : GG::RBOX == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                 : CU_TENSOR_MAP_SWIZZLE_32B;
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Shared memory the epilogue needs (the stage ring is reused); the final merge also keeps
+// two floats per (row, cluster) there, bounded by the splits the planner allows.
+template <int D, int NT>
+constexpr size_t merge_bytes() {
+  constexpr int RG = 8 * NT;
+  return ((size_t)kWarps * RG * 2 + (size_t)kWarps * RG * D + (size_t)RG * D + 2 * RG +
+          3 * kMaxCluster * RG + 2 * RG) *
+         4;
+}
+
 template <typename T, int BITS, int D, int NT>
 int launch_split(const AttnArgs& a, cudaStream_t st) {
-  using C = Cfg<T, BITS, D>;
+  using GG = Geo<BITS, D, 64 * sub_tiles<D, NT>()>;
+  constexpr int RG = 8 * NT;
   const int R = (a.HQ / a.HKV) * a.S;
-  const int RG = 8 * NT;
   const int row_groups = (R + RG - 1) / RG;
-  const size_t ring = (size_t)C::STAGES * C::STAGE_BYTES;
-  const size_t merge = (size_t)kWarps * RG * (D + 2) * 4;
-  const size_t smem = std::max(ring, merge);
-  auto kern = decode_split_kernel<T, BITS, D, NT>;
+  const size_t ring = (size_t)GG::STAGES * GG::STAGE_BYTES;
+  const size_t smem = std::max(ring, merge_bytes<D, NT>()) + 1024;  // + alignment slack
+  DecodeParams p;
+  p.a = a;
+  p.clusters = a.splits / a.cluster;
+  p.gpart = (float*)a.workspace;
+  if (!make_code_map<BITS, D>(&p.tmk, a.kw, a.NP, (long long)a.B * a.HKV) ||
+      !make_code_map<BITS, D>(&p.tmv, a.vw, a.NP, (long long)a.B * a.HKV))
+    return QKV_ECUDA;
+  auto kern = decode_kernel<T, BITS, D, NT>;
   static unsigned attr_done = 0;  // one bit per device, per instantiation
   int dev = 0;
   cudaGetDevice(&dev);
@@ -589,9 +941,21 @@ int launch_split(const AttnArgs& a, cudaStream_t st) {
       return QKV_ECUDA;
     attr_done |= 1u << (dev & 31);
   }
-  dim3 grid(a.splits, a.HKV * row_groups, a.B);
-  kern<<<grid, kThreads, smem, st>>>(a);
-  return QKV_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, a.HKV * row_groups, a.B);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? QKV_OK : QKV_ECUDA;
 }
 
 template <typename T, int BITS, int NT>
@@ -599,7 +963,9 @@ int launch_split_d(const AttnArgs& a, cudaStream_t st) {
   switch (a.D) {
     case 64: return launch_split<T, BITS, 64, NT>(a, st);
     case 128: return launch_split<T, BITS, 128, NT>(a, st);
-    case 256: return launch_split<T, BITS, 256, NT>(a, st);
+    case 256:
+      if constexpr (NT == 1) return launch_split<T, BITS, 256, NT>(a, st);
+      return QKV_EUNSUPPORTED;
     default: return QKV_EUNSUPPORTED;
   }
 }
@@ -609,40 +975,144 @@ int launch_split_b(const AttnArgs& a, cudaStream_t st) {
   return a.bits == 4 ? launch_split_d<T, 4, NT>(a, st) : launch_split_d<T, 8, NT>(a, st);
 }
 
+int launch_split_any(const AttnArgs& a, cudaStream_t st) {
+  const bool nt1 = decode_rows_per_group((a.HQ / a.HKV) * a.S, a.D) == 8;
+  if (a.dtype == QKV_BF16)
+    return nt1 ? launch_split_b<__nv_bfloat16, 1>(a, st) : launch_split_b<__nv_bfloat16, 2>(a, st);
+  return nt1 ? launch_split_b<__half, 1>(a, st) : launch_split_b<__half, 2>(a, st);
+}
+
 }  // namespace
 
-int decode_rows_per_group(int R) { return R <= 8 ? 8 : 16; }
+// 16-row groups (two MMA n-tiles) only where the accumulators fit in registers.
+int decode_rows_per_group(int R, int D) { return (R <= 8 || D > 128) ? 8 : 16; }
 
-void decode_pick_split(int B, int HKV, int row_groups, int n_max, int* splits, int* chunk) {
-  const int units = std::max(1, B * HKV * row_groups);
-  const int target = 2 * num_sms();  // two resident CTAs per SM, one wave
-  int sp = std::max(1, (target + units - 1) / units);
-  const int max_sp = std::max(1, (n_max + kTP - 1) / kTP);
+namespace {
+
+// Co-resident clusters of `cl` CTAs for one decode instantiation on the current device
+// (cached); 0 when the query is unavailable (e.g. no device).
+template <int BITS, int D, int NT>
+int max_clusters(int cl) {
+  using GG = Geo<BITS, D, 64 * sub_tiles<D, NT>()>;
+  constexpr int RG = 8 * NT;
+  static int cache[64][4];
+  static bool init[64][4];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int ci = cl == 8 ? 3 : cl == 4 ? 2 : cl == 2 ? 1 : 0;
+  if (init[dev][ci]) return cache[dev][ci];
+  const size_t ring = (size_t)GG::STAGES * GG::STAGE_BYTES;
+  const size_t smem = std::max(ring, merge_bytes<D, NT>()) + 1024;
+  auto kern = decode_kernel<__nv_bfloat16, BITS, D, NT>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+      cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl * 64, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cache[dev][ci] = n;
+  init[dev][ci] = true;
+  return n;
+}
+
+int max_clusters_any(int bits, int D, int R, int cl) {
+  const bool nt1 = decode_rows_per_group(R, D) == 8;
+#define QKV_MC(BB, DD) \
+  if (bits == BB && D == DD) return nt1 ? max_clusters<BB, DD, 1>(cl) : max_clusters<BB, DD, 2>(cl);
+  QKV_MC(4, 64) QKV_MC(4, 128) QKV_MC(8, 64) QKV_MC(8, 128)
+  if (D == 256) return bits == 4 ? max_clusters<4, 256, 1>(cl) : max_clusters<8, 256, 1>(cl);
+#undef QKV_MC
+  return 0;
+}
+
+int round_chunk(int n_max, int sp) {
+  int ch = (std::max(n_max, 1) + sp - 1) / sp;
+  return std::max(16, (ch + 15) / 16 * 16);  // whole 16-key warp tiles
+}
+
+}  // namespace
+
+// Split plan: as many co-resident CTAs as the GPU holds in one wave, grouped in the
+// largest cluster size that loses at most ~8 % of those slots to cluster packing.
+void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want,
+                 int* splits, int* chunk, int* cluster) {
+  const int R = (HQ / HKV) * S;
+  const int rgs = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
+  const int units = std::max(1, B * HKV * rgs);
+  const int max_sp = std::max(1, (std::max(n_max, 1) + 15) / 16);
+  if (want > 0) {
+    const int sp = want;
+    int cl = 1;
+    while (cl * 2 <= std::min(sp, kMaxCluster) && sp % (cl * 2) == 0) cl *= 2;
+    *splits = std::min(sp, kMaxClustersPerGroup * cl);
+    *cluster = cl;
+    *chunk = round_chunk(n_max, *splits);
+    return;
+  }
+  int best_ctas = 0, best_cl = 1, best_i = 0;
+  int ctas[4] = {0, 0, 0, 0};
+  const int cls[4] = {1, 2, 4, 8};
+  for (int i = 0; i < 4; ++i) {
+    int mc = max_clusters_any(bits, D, R, cls[i]);
+    if (mc <= 0) mc = (i == 0 ? 1 : 0) * (decode_ctas_per_sm(R, D) * num_sms());  // no query
+    ctas[i] = mc * cls[i];
+    if (ctas[i] > best_ctas) best_ctas = ctas[i];
+  }
+  for (int i = 3; i >= 0; --i) {
+    if (ctas[i] > 0 && ctas[i] * 100 >= best_ctas * 92) {
+      best_cl = cls[i];
+      best_i = i;
+      break;
+    }
+  }
+  int slots = ctas[best_i];
+  if (ctas[3] == 0 && ctas[2] == 0 && ctas[1] == 0) {  // no device to ask: heuristic
+    best_cl = 4;
+    slots = ctas[0] / 16 * 15;
+  }
+  slots = std::max(slots, best_cl);
+  int sp = std::max(1, slots / units);
   sp = std::min(sp, max_sp);
-  int ch = (n_max + sp - 1) / sp;
-  ch = std::max(kTP, (ch + kTP - 1) / kTP * kTP);
-  *chunk = ch;
-  *splits = std::max(1, (n_max + ch - 1) / ch);
+  int cl = best_cl;
+  while (cl > 1 && cl > sp) cl /= 2;
+  sp = std::max(cl, sp / cl * cl);
+  sp = std::min(sp, kMaxClustersPerGroup * cl);
+  *splits = sp;
+  *cluster = cl;
+  *chunk = round_chunk(n_max, sp);
 }
 
-size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits) {
+size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster) {
+  return (size_t)(splits / cluster) * B * HQ * S * (D + 4) * sizeof(float);
+}
+
+size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster) {
   (void)HKV;
-  return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
+  return decode_partials_bytes(B, HQ, S, D, splits, cluster);
 }
 
-int launch_split_only(const AttnArgs& a, cudaStream_t st) {
-  const int R = (a.HQ / a.HKV) * a.S;
-  if (a.dtype == QKV_BF16)
-    return R <= 8 ? launch_split_b<__nv_bfloat16, 1>(a, st) : launch_split_b<__nv_bfloat16, 2>(a, st);
-  return R <= 8 ? launch_split_b<__half, 1>(a, st) : launch_split_b<__half, 2>(a, st);
-}
+int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, st); }
 
 int launch_decode(const AttnArgs& a, cudaStream_t st) {
-  const int rc = launch_split_only(a, st);
+  const int rc = launch_split_any(a, st);
   if (rc != QKV_OK) return rc;
   const long long rows = (long long)a.B * a.HQ * a.S;
-  return launch_combine((const float*)a.workspace, a.splits, rows, rows, a.D, a.out, a.dtype,
-                        a.out_kind, st);
+  return launch_combine((const float*)a.workspace, a.splits / a.cluster, rows, rows, a.D, a.out,
+                        a.dtype, a.out_kind, st);
 }
 
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
@@ -651,15 +1121,24 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
   const int warps = kCombineWarps;
   const unsigned grid = (unsigned)rows;
   float* op = out_kind == QKV_OUT_PARTIAL ? (float*)out : nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(warps * 32, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaSuccess;
 #define QKV_C_CASE(DD)                                                                       \
   case DD:                                                                                   \
     if (out_dtype == QKV_BF16)                                                               \
-      combine_kernel<__nv_bfloat16, DD><<<grid, warps * 32, 0, st>>>(                        \
-          parts, n_parts, part_stride_rows, rows, (__nv_bfloat16*)out, op);                  \
+      e = cudaLaunchKernelEx(&cfg, combine_kernel<__nv_bfloat16, DD>, parts, n_parts,        \
+                             part_stride_rows, rows, (__nv_bfloat16*)out, op);               \
     else                                                                                     \
-      combine_kernel<__half, DD><<<grid, warps * 32, 0, st>>>(parts, n_parts,                \
-                                                              part_stride_rows, rows,        \
-                                                              (__half*)out, op);             \
+      e = cudaLaunchKernelEx(&cfg, combine_kernel<__half, DD>, parts, n_parts,               \
+                             part_stride_rows, rows, (__half*)out, op);                      \
     break;
   switch (D) {
     QKV_C_CASE(64)
@@ -669,7 +1148,7 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
       return QKV_EUNSUPPORTED;
   }
 #undef QKV_C_CASE
-  return QKV_OK;
+  return e == cudaSuccess ? QKV_OK : QKV_ECUDA;
 }
 
 }  // namespace qkv

@@ -29,18 +29,27 @@ struct AttnArgs {
   int mask_nk;
   long long mask_sb, mask_sh, mask_sq;
   int out_kind;
-  int splits;  // resolved split count (>= 1)
-  int chunk;   // keys per split (multiple of the stage size)
+  int splits;   // resolved split count (>= 1, a multiple of cluster)
+  int chunk;    // keys per split (multiple of the 16-key warp tile)
+  int cluster;  // CTAs per thread-block cluster along the splits (1..8)
   void* workspace;
   size_t ws_bytes;
   int* status;  // device status word for bounded-wait failures
+  int prefetch_limit;  // cache positions below this may be read before the kernel that
+                       // precedes this one in the stream has finished (see qkv_decode.cu)
 };
 
 // Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
-constexpr int kDecodeStagePos = 64;  // keys per pipeline stage
-int decode_rows_per_group(int R);    // query rows handled by one CTA (8 or 16)
-size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits);
-void decode_pick_split(int B, int HKV, int row_groups, int n_max, int* splits, int* chunk);
+// Upper bound on (batch x kv heads x query-row groups) per call.
+constexpr int kMaxCounters = 16384;
+int decode_rows_per_group(int R, int D);    // query rows handled by one CTA (8 or 16)
+size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster);
+size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster);
+void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want_splits,
+                 int* splits, int* chunk, int* cluster);
+// resident CTAs per SM the decode kernel is built for (register budget per instantiation)
+inline int decode_ctas_per_sm(int R, int D) { return (R <= 8 && D <= 128) ? 3 : 2; }
+
 int launch_decode(const AttnArgs& a, cudaStream_t st);  // split kernel + combine
 int launch_split_only(const AttnArgs& a, cudaStream_t st);  // partial rows into a.workspace
 

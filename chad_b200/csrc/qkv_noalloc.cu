@@ -14,10 +14,10 @@
 // array's name to a kernel, since in host code that name is only a stand-in, not a device
 // address. Make that first call on a device before any stream capture begins.
 //
-// Sharing: every call on a device uses the same array. Each call writes every partial row it
-// later reads, so nothing has to start at zero, but two calls whose kernels overlap on the
-// GPU (for example on two streams at once) race on the array: serialize them. The array
-// keeps the last call's contents.
+// Sharing: every call on a device uses the same array, which keeps the last call's contents.
+// Each call writes every partial row before reading it, so nothing in it has to start at
+// zero. Two calls whose kernels overlap on the GPU (for example on two streams at once) race
+// on the array: serialize them.
 #include <algorithm>
 
 #include "../../include/qkv.h"
@@ -75,9 +75,9 @@ extern "C" int qkv_attention_noalloc(const void* q, const void* kw, const void* 
     if (splits == 0) {
       need = qkv_workspace_size(B, HQ, HKV, S, D, n_max, bits, group_size);
     } else {
-      int ch = (n_max + splits - 1) / splits;
-      ch = std::max(kDecodeStagePos, (ch + kDecodeStagePos - 1) / kDecodeStagePos * kDecodeStagePos);
-      need = decode_workspace_bytes(B, HQ, HKV, S, D, std::max(1, (n_max + ch - 1) / ch));
+      int sp = 1, ch = 16, cl = 1;
+      decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &sp, &ch, &cl);
+      need = decode_workspace_bytes(B, HQ, HKV, S, D, sp, cl);
     }
     if (need > kNoAllocScratchBytes)
       return set_last_error(QKV_EWORKSPACE,
