@@ -155,7 +155,13 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
   (void)rg;
   int splits = 1, chunk = 16, cluster = 1;
   decode_plan(B, HQ, HKV, S, D, bits, std::max(n_max, 1), 0, &splits, &chunk, &cluster);
-  return decode_workspace_bytes(B, HQ, HKV, S, D, splits, cluster);
+  size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, splits, cluster);
+  // multi-token calls may take the tensor-core path: room for its split partials too
+  if (prefill_tc_eligible(B, HQ, HKV, S, D, nullptr, nullptr, nullptr, QKV_MASK_CAUSAL)) {
+    const TcPlan tp = prefill_tc_plan(B, HQ, HKV, S, std::max(n_max, 1), 0);
+    need = std::max(need, prefill_tc_workspace_bytes(B, HQ, S, D, tp, false));
+  }
+  return need;
 }
 
 namespace {
@@ -167,7 +173,7 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
                const int* total_lens, int bits, int group_size, int dtype, float scale,
                int mask_kind, const void* mask, int mask_nk, long long mask_sb,
                long long mask_sh, long long mask_sq, int splits, void* workspace,
-               size_t ws_bytes) {
+               size_t ws_bytes, bool direct) {
   int rc = check_cache_shape(D, bits, group_size);
   if (rc) return rc;
   if (!q || !kw || !ks || !kb || !vw || !vs || !vb || !out)
@@ -232,7 +238,12 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
     return fail(QKV_EUNSUPPORTED, "too many query-row groups (%lld > %d)",
                 (long long)B * HKV * rg, kMaxCounters);
   decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
-  const size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
+  size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
+  a.use_tc = prefill_tc_eligible(B, HQ, HKV, S, D, lens, pos_base, total_lens, a.mask_kind);
+  if (a.use_tc) {
+    a.tc = prefill_tc_plan(B, HQ, HKV, S, n_max, splits);
+    need = prefill_tc_workspace_bytes(B, HQ, S, D, a.tc, direct);
+  }
   if (!workspace || ws_bytes < need)
     return fail(QKV_EWORKSPACE, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (!aligned16(workspace)) return fail(QKV_EALIGN, "workspace must be 16-byte aligned");
@@ -255,10 +266,12 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
   AttnArgs a;
   int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, n, lens,
                       pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
-                      mask_nk, mask_sb, mask_sh, mask_sq, splits, workspace, ws_bytes);
+                      mask_nk, mask_sb, mask_sh, mask_sq, splits, workspace, ws_bytes,
+                      out_kind == QKV_OUT_NORMALIZED);
   if (rc) return rc;
   a.out_kind = out_kind;
-  rc = launch_decode(a, static_cast<cudaStream_t>(stream));
+  rc = a.use_tc ? launch_prefill_tc(a, a.tc, true, static_cast<cudaStream_t>(stream))
+                : launch_decode(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "attention: unsupported configuration");
   return cuda_check("qkv_attention");
 }
@@ -274,11 +287,12 @@ int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, 
   AttnArgs a;
   int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, parts, B, HQ, HKV, S, D, NP, n, lens,
                       pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
-                      mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes);
+                      mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes, false);
   if (rc) return rc;
   a.out_kind = QKV_OUT_PARTIAL;
-  *n_parts = a.splits / a.cluster;
-  rc = launch_split_only(a, static_cast<cudaStream_t>(stream));
+  *n_parts = a.use_tc ? a.tc.splits : a.splits / a.cluster;
+  rc = a.use_tc ? launch_prefill_tc(a, a.tc, false, static_cast<cudaStream_t>(stream))
+                : launch_split_only(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "partials: unsupported configuration");
   return cuda_check("qkv_partials");
 }

@@ -60,12 +60,22 @@ __device__ __forceinline__ int key_perm(int k) {
   return (k & 8) | p;
 }
 
-// 16-key sub-tiles per consumer warp per stage: two where registers allow, so a warp runs
-// two independent MMA chains and shares one softmax reduction between them.
-template <int D, int NT>
-constexpr int sub_tiles() { return (NT == 1 && D <= 128) ? 2 : 1; }
+// Per-instantiation shape of the decode kernel.
+//   SUB   16-key sub-tiles per consumer warp per stage: two where registers allow, so a
+//         warp runs two independent MMA chains and shares one softmax reduction.
+//   CTAS  CTAs resident per SM (register cap through __launch_bounds__).
+//   RING  shared-memory budget of the stage ring, so that CTAS CTAs fit in the SM's
+//         228 KB with their static arrays, the alignment slack and 1 KB reserved each.
+template <int BITS, int D, int NT>
+struct DecodeCfg {
+  static constexpr bool kNarrow = NT == 1 && D <= 128;
+  static constexpr int SUB = kNarrow && BITS == 4 ? 2 : 1;
+  static constexpr int CTAS = kNarrow ? 3 : 2;
+  static constexpr int TP = 64 * SUB;  // keys per stage
+  static constexpr int RING = CTAS == 3 ? 64 * 1024 : 104 * 1024;
+};
 
-template <int BITS, int D, int TP>
+template <int BITS, int D, int TP, int RING = 72 * 1024>
 struct Geo {
   static constexpr int G = D / 64;                   // scale groups per row
   static constexpr int RB = D * BITS / 8;            // code bytes per key
@@ -85,14 +95,13 @@ struct Geo {
   static constexpr int OFF_VS = OFF_KB + SC_BYTES;
   static constexpr int OFF_VB = OFF_VS + SC_BYTES;
   static constexpr int STAGE_BYTES = ((OFF_VB + SC_BYTES) + 1023) / 1024 * 1024;
-  static constexpr int STAGES = STAGE_BYTES * 4 <= 72 * 1024 ? 4
-                                : STAGE_BYTES * 3 <= 72 * 1024 ? 3 : 2;
+  static constexpr int STAGES = STAGE_BYTES * 4 <= RING ? 4 : STAGE_BYTES * 3 <= RING ? 3 : 2;
 };
 
 // Byte offset of (key row, code byte) inside a swizzled code tile.
-template <int BITS, int D, int TP>
+template <int BITS, int D, int TP, int RING>
 __device__ __forceinline__ int code_off(int key, int byte) {
-  using g = Geo<BITS, D, TP>;
+  using g = Geo<BITS, D, TP, RING>;
   const int sub = byte / g::RBOX;
   const int lin = key * g::RBOX + (byte % g::RBOX);
   return sub * (TP * g::RBOX) + (lin ^ (((lin >> 7) & g::SWZ) << 4));
@@ -184,10 +193,11 @@ struct DecodeParams {
 };
 
 template <typename T, int BITS, int D, int NT>
-__global__ void __launch_bounds__(kThreads, (NT == 1 && D <= 128) ? 3 : 2) decode_kernel(const __grid_constant__ DecodeParams P) {
-  constexpr int kSub = sub_tiles<D, NT>();
-  constexpr int kTP = 64 * kSub;  // keys per stage
-  using GG = Geo<BITS, D, kTP>;
+__global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode_kernel(const __grid_constant__ DecodeParams P) {
+  using CF = DecodeCfg<BITS, D, NT>;
+  constexpr int kSub = CF::SUB;
+  constexpr int kTP = CF::TP;  // keys per stage
+  using GG = Geo<BITS, D, kTP, CF::RING>;
   constexpr int G = GG::G;
   constexpr int RG = 8 * NT;  // query rows per CTA
   constexpr int KS = 4;       // k-steps (and m-tiles) per scale group
@@ -423,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && D <= 128) ? 3 : 2) decod
 #pragma unroll
           for (int h = 0; h < kSub; ++h) {
             uint32_t wa[GG::KW], wb[GG::KW];
-            lds_words<GG::KW>(wa, st + GG::OFF_KC + code_off<BITS, D, kTP>(t0 + 16 * h + kA, g * GG::GB + tq * GG::KLB));
-            lds_words<GG::KW>(wb, st + GG::OFF_KC + code_off<BITS, D, kTP>(t0 + 16 * h + kB, g * GG::GB + tq * GG::KLB));
+            lds_words<GG::KW>(wa, st + GG::OFF_KC + code_off<BITS, D, kTP, CF::RING>(t0 + 16 * h + kA, g * GG::GB + tq * GG::KLB));
+            lds_words<GG::KW>(wb, st + GG::OFF_KC + code_off<BITS, D, kTP, CF::RING>(t0 + 16 * h + kB, g * GG::GB + tq * GG::KLB));
             if constexpr (BITS == 4) {
 #pragma unroll
               for (int u = 0; u < GG::KW; ++u) {
@@ -599,10 +609,10 @@ __global__ void __launch_bounds__(kThreads, (NT == 1 && D <= 128) ? 3 : 2) decod
             uint32_t w0[GG::VW], w1[GG::VW], w2[GG::VW], w3[GG::VW];
             const int vb0 = g * GG::GB + gq * GG::VLB;
             const int tr = t0 + 16 * h;
-            lds_words<GG::VW>(w0, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v0k, vb0));
-            lds_words<GG::VW>(w1, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v1k, vb0));
-            lds_words<GG::VW>(w2, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v2k, vb0));
-            lds_words<GG::VW>(w3, st + GG::OFF_VC + code_off<BITS, D, kTP>(tr + v3k, vb0));
+            lds_words<GG::VW>(w0, st + GG::OFF_VC + code_off<BITS, D, kTP, CF::RING>(tr + v0k, vb0));
+            lds_words<GG::VW>(w1, st + GG::OFF_VC + code_off<BITS, D, kTP, CF::RING>(tr + v1k, vb0));
+            lds_words<GG::VW>(w2, st + GG::OFF_VC + code_off<BITS, D, kTP, CF::RING>(tr + v2k, vb0));
+            lds_words<GG::VW>(w3, st + GG::OFF_VC + code_off<BITS, D, kTP, CF::RING>(tr + v3k, vb0));
             if constexpr (BITS == 4) {
               const uint32_t xa = prmt(w0[0], w1[0], 0x5410), ya = prmt(w0[0], w1[0], 0x7632);
               const uint32_t xb = prmt(w2[0], w3[0], 0x5410), yb = prmt(w2[0], w3[0], 0x7632);
@@ -892,18 +902,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int BITS, int D>
 bool make_code_map(CUtensorMap* m, const void* base, int NP, long long bhs) {
   using GG = Geo<BITS, D, kBoxRows>;
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {(cuuint64_t)GG::RB, (cuuint64_t)NP, (cuuint64_t)bhs};
-  const cuuint64_t strides[2] = {(cuuint64_t)GG::RB, (cuuint64_t)GG::RB * (cuuint64_t)NP};
-  const cuuint32_t box[3] = {(cuuint32_t)GG::RBOX, (cuuint32_t)kBoxRows, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw = GG::RBOX == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : GG::RBOX == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                 : CU_TENSOR_MAP_SWIZZLE_32B;
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_code_map_bytes(m, base, GG::RB, NP, bhs, GG::RBOX, kBoxRows);
 }
 
 // Shared memory the epilogue needs (the stage ring is reused); the final merge also keeps
@@ -918,7 +917,8 @@ constexpr size_t merge_bytes() {
 
 template <typename T, int BITS, int D, int NT>
 int launch_split(const AttnArgs& a, cudaStream_t st) {
-  using GG = Geo<BITS, D, 64 * sub_tiles<D, NT>()>;
+  using CF = DecodeCfg<BITS, D, NT>;
+  using GG = Geo<BITS, D, CF::TP, CF::RING>;
   constexpr int RG = 8 * NT;
   const int R = (a.HQ / a.HKV) * a.S;
   const int row_groups = (R + RG - 1) / RG;
@@ -993,7 +993,8 @@ namespace {
 // (cached); 0 when the query is unavailable (e.g. no device).
 template <int BITS, int D, int NT>
 int max_clusters(int cl) {
-  using GG = Geo<BITS, D, 64 * sub_tiles<D, NT>()>;
+  using CF = DecodeCfg<BITS, D, NT>;
+  using GG = Geo<BITS, D, CF::TP, CF::RING>;
   constexpr int RG = 8 * NT;
   static int cache[64][4];
   static bool init[64][4];
@@ -1149,6 +1150,24 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
   }
 #undef QKV_C_CASE
   return e == cudaSuccess ? QKV_OK : QKV_ECUDA;
+}
+
+// Byte-typed tiled tensor map over (RB, NP, bhs) codes, box (box_inner bytes, box_rows
+// keys, 1), swizzled by the box's inner span (32, 64 or 128 bytes).
+bool make_code_map_bytes(CUtensorMap* m, const void* base, int RB, int NP, long long bhs,
+                         int box_inner, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)RB, (cuuint64_t)NP, (cuuint64_t)bhs};
+  const cuuint64_t strides[2] = {(cuuint64_t)RB, (cuuint64_t)RB * (cuuint64_t)NP};
+  const cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = box_inner == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : box_inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace qkv

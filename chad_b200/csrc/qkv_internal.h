@@ -1,10 +1,21 @@
 // Internal launch interface shared by the kernel translation units and the C-ABI layer.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
 namespace qkv {
+
+// Tensor-core (tcgen05) path for multi-token attention over the quantized cache: head_dim
+// 128, GQA dividing 128, no mask or causal, one length for every batch row.
+struct TcPlan {
+  int tokens_per_tile;  // query tokens of one GQA group in a 128-row MMA tile
+  int tiles;            // 128-row tiles per CTA (1 or 2)
+  int tblocks;          // CTAs along the query tokens
+  int splits;           // CTAs along the keys
+  int chunk;            // keys per split (multiple of 64)
+};
 
 // Everything one attention launch needs (device pointers; sizes already validated).
 struct AttnArgs {
@@ -37,6 +48,8 @@ struct AttnArgs {
   int* status;  // device status word for bounded-wait failures
   int prefetch_limit;  // cache positions below this may be read before the kernel that
                        // precedes this one in the stream has finished (see qkv_decode.cu)
+  bool use_tc;         // multi-token tensor-core path (qkv_prefill_tc.cu) instead of decode
+  TcPlan tc;
 };
 
 // Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
@@ -63,6 +76,20 @@ int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, 
                       int D, int bits, int dtype, int round_mode, cudaStream_t st);
 
 int num_sms();
+
+// Byte-typed tiled tensor map over (RB, NP, bhs) packed codes; box (box_inner bytes,
+// box_rows keys, 1), swizzled by the box's inner span. False if the driver refuses it.
+bool make_code_map_bytes(CUtensorMap* m, const void* base, int RB, int NP, long long bhs,
+                         int box_inner, int box_rows);
+
+
+bool prefill_tc_eligible(int B, int HQ, int HKV, int S, int D, const int* lens,
+                         const int* pos_base, const int* total_lens, int mask_kind);
+TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits);
+// Partial rows of every split (none when one split writes the normalized output directly).
+size_t prefill_tc_workspace_bytes(int B, int HQ, int S, int D, const TcPlan& p, bool direct);
+// combine = false leaves the split partials in a.workspace ([splits][B*HQ*S][D+4]).
+int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st);
 
 // Record a message for qkv_last_error() on this thread and return `code`.
 int set_last_error(int code, const char* fmt, ...);
