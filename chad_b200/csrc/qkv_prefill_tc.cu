@@ -44,6 +44,7 @@ constexpr int kKT = 64;          // keys per tile (MMA N of Q K^T)
 constexpr int kWarpsTc = 14;
 constexpr int kThreadsTc = kWarpsTc * 32;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kPolyEvery = 0;  // > 0: one exp2 in kPolyEvery on the FMA pipe, not the MUFU
 #define kNegInfTc (-__int_as_float(0x7f800000))
 
 template <int BITS>
@@ -120,6 +121,17 @@ struct Pack16<__half> {
     return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
   }
 };
+
+// 2^t on the FMA/ALU pipes: t = n + f with n = rint(t), |f| <= 1/2; 2^f from a degree-3
+// polynomial fitted here to relative error 8e-5 over [-1/2, 1/2] (far below the 16-bit P it
+// feeds), 2^n added to the exponent bits. t is clamped at -126: 2^-126 stands in for 0.
+__device__ __forceinline__ float exp2_poly(float t) {
+  t = fmaxf(t, -126.0f);
+  const float j = t + 12582912.0f;        // 1.5 * 2^23: low mantissa bits hold rint(t)
+  const float f = t - (j - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
 
 // code (exact, in T) pair -> round(code * s + b), one rounding, both halves
 template <typename T>
@@ -365,10 +377,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           if (kbase + 32 + i > lim) y[i] = __float_as_uint(kNegInfTc);
         }
       }
-      float mx = kNegInfTc;
+      // row max: eight independent chains, then a tree
+      float mxa[8];
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        mx = fmaxf(mx, fmaxf(__uint_as_float(x[i]), __uint_as_float(y[i])));
+      for (int i = 0; i < 8; ++i) mxa[i] = fmaxf(__uint_as_float(x[i]), __uint_as_float(y[i]));
+#pragma unroll
+      for (int i = 8; i < 32; ++i)
+        mxa[i & 7] = fmaxf(mxa[i & 7], fmaxf(__uint_as_float(x[i]), __uint_as_float(y[i])));
+      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       const float m_cand = mx * c;
       float alpha = 1.f;
       const bool resc = m_cand > m_run + kRescaleLog2;  // false while the tile is all masked
@@ -377,29 +394,34 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         m_run = m_cand;
       }
       const float mu = m_run == kNegInfTc ? 0.f : m_run;
-      float sum = 0.f;
+      // p = 2^(s*c - mu) on the MUFU (or, with kPolyEvery > 0, partly by the polynomial)
+      float sa[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(x[2 * i]), c, -mu));
-        const float p1 = ex2(fmaf(__uint_as_float(x[2 * i + 1]), c, -mu));
-        sum += p0 + p1;
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t* src = i < 16 ? x : y;
+        const int e = (i & 15) * 2;
+        const float t0 = fmaf(__uint_as_float(src[e]), c, -mu);
+        const float t1 = fmaf(__uint_as_float(src[e + 1]), c, -mu);
+        const float p0 = (kPolyEvery > 0 && (2 * i) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(t0) : ex2(t0);
+        const float p1 = (kPolyEvery > 0 && (2 * i + 1) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(t1) : ex2(t1);
+        sa[(2 * i) & 3] += p0;
+        sa[(2 * i + 1) & 3] += p1;
         pk[i] = PK::pack(p0, p1);
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float p0 = ex2(fmaf(__uint_as_float(y[2 * i]), c, -mu));
-        const float p1 = ex2(fmaf(__uint_as_float(y[2 * i + 1]), c, -mu));
-        sum += p0 + p1;
-        pk[16 + i] = PK::pack(p0, p1);
-      }
+      const float sum = (sa[0] + sa[1]) + (sa[2] + sa[3]);
       l_run = fmaf(l_run, alpha, sum);
       tc::st32(ts, pk);  // P (16-bit pairs) over the first 32 columns of S
       tc::wait_st();
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        // O must not be in flight: wait for PV(j-1), then scale this row in place
+      if (j > 0) {
+        // Wait for PV(j-1) on every tile: a parity wait only tells phases apart while the
+        // barrier is at most one phase ahead of this thread's view of it, and a rescale
+        // needs O out of flight anyway. PV(j-1) normally finished during this softmax.
         ok = mbar_wait(&o_done[m], (j - 1) & 1, a.status, 45);
         if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        // scale this row of O in place (PV(j) is not issued before p_full below)
         tc::fence_after_sync();
         const uint32_t to = tmem + lane_off + 256 + m * 128;
 #pragma unroll 1

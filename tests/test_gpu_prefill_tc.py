@@ -128,3 +128,14 @@ def test_prefill_entry_point_uses_cache_append():
                       D ** -0.5)
     _check(out, _ref(q, k, v, 4, "bf16", prefix + S, "causal"))
     assert ops.device_status() == 0
+
+
+def test_repeated_calls_are_bit_identical():
+    """The pipeline's barriers order every tensor-memory read after the MMA writing it, so
+    repeated calls give identical bits (a missed wait shows up as run-to-run noise)."""
+    S, n = 256, 4000 + 256
+    q, k, v = make_case(44, 1, 32, 4, S, 128, n, "bf16", outliers=True)
+    c = _cache(k, v, 4, "bf16")
+    first = _run(q, c, n, 4, "bf16", "causal", splits=1)
+    for _ in range(6):
+        assert torch.equal(first, _run(q, c, n, 4, "bf16", "causal", splits=1))
