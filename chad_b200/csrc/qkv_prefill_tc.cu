@@ -56,12 +56,14 @@ struct TcGeo {
   static constexpr int NST = BITS == 4 ? 4 : 3;
 };
 
+constexpr int kKvBufs = 3;  // dequantized K/V tile buffers: dequant runs up to 2 tiles ahead
+
 template <int BITS, int MT>
 struct TcSmem {
   static constexpr int Q = 0;                       // MT x (2 halves x 128 rows x 128 B)
-  static constexpr int KD = MT * 32768;             // 2 buffers x (2 halves x 64 keys x 128 B)
-  static constexpr int VD = KD + 2 * 16384;         // 2 buffers, same layout (MN-major V)
-  static constexpr int RING = VD + 2 * 16384;
+  static constexpr int KD = MT * 32768;             // kKvBufs x (2 halves x 64 keys x 128 B)
+  static constexpr int VD = KD + kKvBufs * 16384;   // same layout (MN-major V)
+  static constexpr int RING = VD + kKvBufs * 16384;
   static constexpr int BYTES = RING + TcGeo<BITS>::NST * TcGeo<BITS>::STAGE;
 };
 
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint64_t code_full[GE::NST], code_empty[GE::NST];
-  __shared__ uint64_t kv_full[2], kv_empty[2];
+  __shared__ uint64_t kv_full[kKvBufs], kv_empty[kKvBufs];
   __shared__ uint64_t s_full[MT][2], p_full[MT][2], o_done[MT];
   __shared__ uint64_t mma_fin;
   __shared__ uint32_t tmem_sh;
@@ -236,9 +238,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       mbar_init(&code_full[s], 1);
       mbar_init(&code_empty[s], 4);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKvBufs; ++s) {
       mbar_init(&kv_full[s], 4);
       mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       for (int m = 0; m < MT; ++m) {
         mbar_init(&s_full[m][s], 1);
         mbar_init(&p_full[m][s], 4);
@@ -311,24 +315,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       const uint32_t kd_base = smem_u32(smem + SM::KD);
       const uint32_t vd_base = smem_u32(smem + SM::VD);
       auto issue_pv = [&](int jj) {
-        const int pb = jj & 1;
+        const int pb = jj & 1;            // S / P buffer
+        const int vb = jj % kKvBufs;      // V buffer
         for (int m = 0; m < MT && ok; ++m) {
           ok = mbar_wait(&p_full[m][pb], (jj >> 1) & 1, a.status, 41);
           if (!ok) break;
           tc::fence_after_sync();
 #pragma unroll
           for (int s = 0; s < 4; ++s) {
-            const uint64_t bd = tc::sdesc_sw128(vd_base + pb * 16384 + s * 2048, 8192, 1024);
+            const uint64_t bd = tc::sdesc_sw128(vd_base + vb * 16384 + s * 2048, 8192, 1024);
             tc::mma_ts(tmem + 256 + m * 128, tmem + m * 128 + pb * 64 + s * 8, bd, id_o,
                        (jj > 0 || s > 0) ? 1u : 0u);
           }
           tc::mma_commit(&o_done[m]);
         }
-        tc::mma_commit(&kv_empty[pb]);
+        tc::mma_commit(&kv_empty[vb]);
       };
       for (int j = 0; j < ntiles && ok; ++j) {
-        const int buf = j & 1;
-        ok = mbar_wait(&kv_full[buf], (j >> 1) & 1, a.status, 42);
+        const int buf = j % kKvBufs, sb = j & 1;
+        ok = mbar_wait(&kv_full[buf], (j / kKvBufs) & 1, a.status, 42);
         if (!ok) break;
         tc::fence_after_sync();
         for (int m = 0; m < MT; ++m) {
@@ -338,9 +343,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
                 tc::sdesc_sw128(q_base + m * 32768 + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
             const uint64_t bd =
                 tc::sdesc_sw128(kd_base + buf * 16384 + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024);
-            tc::mma_ss(tmem + m * 128 + buf * 64, ad, bd, id_s, s > 0 ? 1u : 0u);
+            tc::mma_ss(tmem + m * 128 + sb * 64, ad, bd, id_s, s > 0 ? 1u : 0u);
           }
-          tc::mma_commit(&s_full[m][buf]);
+          tc::mma_commit(&s_full[m][sb]);
         }
         if (j > 0) issue_pv(j - 1);
       }
@@ -495,7 +500,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     const int row = dq & 63;
     uint8_t* dst_base = smem + (is_v ? SM::VD : SM::KD);
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j % GE::NST, buf = j & 1;
+      const int st = j % GE::NST, buf = j % kKvBufs;
       ok = mbar_wait(&code_full[st], (j / GE::NST) & 1, a.status, 47);
       if (!__all_sync(0xffffffffu, ok)) break;
       const uint8_t* sp = smem + SM::RING + st * GE::STAGE;
@@ -516,8 +521,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       if (lane == 0) mbar_arrive(&code_empty[st]);
       const uint32_t s0 = prmt(sc, 0u, 0x1010), s1 = prmt(sc, 0u, 0x3232);
       const uint32_t b0 = prmt(bi, 0u, 0x1010), b1 = prmt(bi, 0u, 0x3232);
-      if (j >= 2) {
-        ok = mbar_wait(&kv_empty[buf], ((j >> 1) + 1) & 1, a.status, 48);
+      if (j >= kKvBufs) {  // PV(j - kKvBufs) released this buffer
+        ok = mbar_wait(&kv_empty[buf], ((j / kKvBufs) + 1) & 1, a.status, 48);
         if (!__all_sync(0xffffffffu, ok)) break;
       }
       uint8_t* dst = dst_base + buf * 16384;
