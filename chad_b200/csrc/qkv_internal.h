@@ -14,7 +14,7 @@ struct TcPlan {
   int tiles;            // 128-row tiles per CTA (1 or 2)
   int tblocks;          // CTAs along the query tokens
   int splits;           // CTAs along the keys
-  int chunk;            // keys per split (multiple of 64)
+  int chunk;            // keys per split (multiple of the 128-key tile)
 };
 
 // Everything one attention launch needs (device pointers; sizes already validated).

@@ -7,14 +7,16 @@
 //
 //   * CTA = up to two 128-row MMA tiles of query rows of ONE kv head: row r of a tile is
 //     (q head r / TT of the GQA group, token r % TT), TT = 128 / GQA; every row of the CTA
-//     shares each dequantized K/V tile.
-//   * Warp roles (14 warps): 0 TMA producer (packed codes, scales, biases), 1 tensor-memory
-//     owner and single-thread MMA issuer, 2-3 and 12-13 dequantizers (codes -> 16-bit K/V
-//     tiles in the 128-byte-swizzled operand layout), 4-7 / 8-11 softmax of tile 0 / 1.
-//   * Per 64-key tile j: S_m = Q_m K^T (tcgen05, K-major operands) into tensor memory;
-//     softmax threads own one S row each (no cross-thread reductions), write P (16-bit)
-//     back over S and the MMA warp accumulates O_m += P_m V with P read from tensor memory
-//     and V as an MN-major operand. S is double-buffered so QK(j+1) overlaps softmax(j).
+//     shares each dequantized K/V tile of 128 keys.
+//   * Warp roles (13 warps): 0 tensor-memory owner and single-thread MMA issuer; 1-3 and 12
+//     dequantizers (packed codes read from global memory, one key row of K and of V per
+//     thread, written as 16-bit tiles in the 128-byte-swizzled operand layout); 4-7 / 8-11
+//     softmax of tile 0 / 1 (one S row per thread, no cross-thread reductions).
+//   * Tensor memory: S_0, S_1 (128 columns each, P written back over them as 16-bit pairs),
+//     O_0, O_1 (128 columns each). Per key tile i the MMA thread issues, for each tile m,
+//     O_m += P_m V(i) as soon as softmax_m(i) is done and then S_m = Q_m K(i+1)^T, so one
+//     tile's softmax overlaps the other tile's MMAs (ping-pong). MMAs are M=128, N=128, K=16
+//     (N=64 runs at two thirds of the tensor pipe's rate on B200).
 //   * The running max is only raised when it grows by more than 2^8 (log2 units), so the
 //     O rescale in tensor memory is rare; P values stay <= 256.
 //
@@ -40,36 +42,25 @@ namespace qkv {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kKT = 64;          // keys per tile (MMA N of Q K^T)
-constexpr int kWarpsTc = 14;
+constexpr int kKT = 128;         // keys per tile (MMA N of Q K^T)
+constexpr int kWarpsTc = 13;
 constexpr int kThreadsTc = kWarpsTc * 32;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyEvery = 0;  // > 0: one exp2 in kPolyEvery on the FMA pipe, not the MUFU
+constexpr int kHalf = kKT * 128;       // bytes of one 64-dim half of a K or V tile
+constexpr int kTileBytes = 2 * kHalf;  // one dequantized K or V tile
 #define kNegInfTc (-__int_as_float(0x7f800000))
 
-template <int BITS>
-struct TcGeo {
-  static constexpr int RB = kD * BITS / 8;       // code bytes per key
-  static constexpr int CODE = kKT * RB;          // one code tile
-  static constexpr int SC = kKT * 2 * 2;         // one scale / bias array (2 groups, 16-bit)
-  static constexpr int STAGE = 2 * CODE + 4 * SC;  // multiple of 1024
-  static constexpr int NST = BITS == 4 ? 4 : 3;
-};
-
-constexpr int kKvBufs = 3;  // dequantized K/V tile buffers: dequant runs up to 2 tiles ahead
-
-template <int BITS, int MT>
+template <int MT>
 struct TcSmem {
-  static constexpr int Q = 0;                       // MT x (2 halves x 128 rows x 128 B)
-  static constexpr int KD = MT * 32768;             // kKvBufs x (2 halves x 64 keys x 128 B)
-  static constexpr int VD = KD + kKvBufs * 16384;   // same layout (MN-major V)
-  static constexpr int RING = VD + kKvBufs * 16384;
-  static constexpr int BYTES = RING + TcGeo<BITS>::NST * TcGeo<BITS>::STAGE;
+  static constexpr int Q = 0;                     // MT x (2 halves x 128 rows x 128 B)
+  static constexpr int KD = MT * 32768;           // 2 buffers of K (K-major operand)
+  static constexpr int VD = KD + 2 * kTileBytes;  // 2 buffers of V (MN-major operand)
+  static constexpr int BYTES = VD + 2 * kTileBytes;
 };
 
 struct TcParams {
   AttnArgs a;
-  CUtensorMap tmk, tmv;
   int TT;        // tokens per 128-row tile
   int chunk;     // keys per split
   float* parts;  // [splits][B*HQ*S][D+4] or nullptr (direct normalized output)
@@ -159,7 +150,7 @@ __device__ __forceinline__ void dequant_row(const uint32_t* words, uint32_t s0, 
       o.z = deq_pair<T>(P::sub(and_or(w >> 8, 0x000F000Fu, magic), magic), s2, b2);   // (2,6)
       o.w = deq_pair<T>(P::sub(and_or(w >> 12, 0x000F000Fu, magic), magic), s2, b2);  // (3,7)
       const int h = i >> 3, c = (i & 7) ^ (row & 7);
-      *reinterpret_cast<uint4*>(dst + h * 8192 + row * 128 + c * 16) = o;
+      *reinterpret_cast<uint4*>(dst + h * kHalf + row * 128 + c * 16) = o;
     }
   } else {
 #pragma unroll
@@ -188,31 +179,36 @@ __device__ __forceinline__ void dequant_row(const uint32_t* words, uint32_t s0, 
       o.z = deq_pair<T>(c[2], s2, b2);
       o.w = deq_pair<T>(c[3], s2, b2);
       const int h = i >> 3, cc = (i & 7) ^ (row & 7);
-      *reinterpret_cast<uint4*>(dst + h * 8192 + row * 128 + cc * 16) = o;
+      *reinterpret_cast<uint4*>(dst + h * kHalf + row * 128 + cc * 16) = o;
     }
   }
 }
 
-__device__ __forceinline__ void tma_load_3d_tc(void* dst, const CUtensorMap* map, int x, int y,
-                                               int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
+// 16-byte read-only global load (codes and scales are immutable during the kernel)
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg4(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
 }
 
 template <typename T, int BITS, int MT>
 __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_constant__ TcParams P) {
-  using GE = TcGeo<BITS>;
-  using SM = TcSmem<BITS, MT>;
+  using SM = TcSmem<MT>;
   using PK = Pack16<T>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int RB = kD * BITS / 8;  // code bytes per key
+  constexpr int RW = RB / 4;         // code words per key
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t code_full[GE::NST], code_empty[GE::NST];
-  __shared__ uint64_t kv_full[kKvBufs], kv_empty[kKvBufs];
-  __shared__ uint64_t s_full[MT][2], p_full[MT][2], o_done[MT];
+  __shared__ uint64_t k_full[2], k_free[2], v_full[2], v_free[2];
+  __shared__ uint64_t s_full[MT], p_full[MT], o_done[MT];
   __shared__ uint64_t mma_fin;
   __shared__ uint32_t tmem_sh;
 
@@ -234,25 +230,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   const int ntiles = k_stop > k_begin ? (k_stop - k_begin + kKT - 1) / kKT : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GE::NST; ++s) {
-      mbar_init(&code_full[s], 1);
-      mbar_init(&code_empty[s], 4);
-    }
-    for (int s = 0; s < kKvBufs; ++s) {
-      mbar_init(&kv_full[s], 4);
-      mbar_init(&kv_empty[s], 1);
-    }
     for (int s = 0; s < 2; ++s) {
-      for (int m = 0; m < MT; ++m) {
-        mbar_init(&s_full[m][s], 1);
-        mbar_init(&p_full[m][s], 4);
-      }
+      mbar_init(&k_full[s], 4);
+      mbar_init(&v_full[s], 4);
+      mbar_init(&k_free[s], 1);
+      mbar_init(&v_free[s], 1);
     }
-    for (int m = 0; m < MT; ++m) mbar_init(&o_done[m], 1);
+    for (int m = 0; m < MT; ++m) {
+      mbar_init(&s_full[m], 1);
+      mbar_init(&p_full[m], 4);
+      mbar_init(&o_done[m], 1);
+    }
     mbar_init(&mma_fin, 1);
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 0) {
     tc::tmem_alloc(&tmem_sh, 512);
     tc::tmem_relinquish();
   }
@@ -286,27 +278,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j % GE::NST;
-        if (j >= GE::NST) ok = mbar_wait(&code_empty[st], ((j / GE::NST) + 1) & 1, a.status, 40);
-        if (!ok) break;
-        const int p0 = k_begin + j * kKT;
-        const int rows = min(kKT, a.NP - p0);
-        const uint32_t sb = rows * 2 * 2;
-        uint8_t* sp = smem + SM::RING + st * GE::STAGE;
-        mbar_arrive_expect_tx(&code_full[st], 2 * GE::CODE + 4 * sb);
-        tma_load_3d_tc(sp, &P.tmk, 0, p0, bh, &code_full[st]);
-        tma_load_3d_tc(sp + GE::CODE, &P.tmv, 0, p0, bh, &code_full[st]);
-        const long long so = ((long long)bh * a.NP + p0) * 2 * 2;
-        bulk_g2s(sp + 2 * GE::CODE, (const uint8_t*)a.ks + so, sb, &code_full[st]);
-        bulk_g2s(sp + 2 * GE::CODE + GE::SC, (const uint8_t*)a.kb + so, sb, &code_full[st]);
-        bulk_g2s(sp + 2 * GE::CODE + 2 * GE::SC, (const uint8_t*)a.vs + so, sb, &code_full[st]);
-        bulk_g2s(sp + 2 * GE::CODE + 3 * GE::SC, (const uint8_t*)a.vb + so, sb, &code_full[st]);
-      }
-    }
-  } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = tc::idesc_f16(kBf16, 128, kKT, false, false);
@@ -314,44 +285,58 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       const uint32_t q_base = smem_u32(smem + SM::Q);
       const uint32_t kd_base = smem_u32(smem + SM::KD);
       const uint32_t vd_base = smem_u32(smem + SM::VD);
-      auto issue_pv = [&](int jj) {
-        const int pb = jj & 1;            // S / P buffer
-        const int vb = jj % kKvBufs;      // V buffer
+      auto qk = [&](int m, int i) {  // S_m = Q_m K(i)^T
+        const uint32_t kb = kd_base + (i & 1) * kTileBytes;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint64_t ad =
+              tc::sdesc_sw128(q_base + m * 32768 + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(kb + (s >> 2) * kHalf + (s & 3) * 32, 16, 1024);
+          tc::mma_ss(tmem + m * 128, ad, bd, id_s, s > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&s_full[m]);
+      };
+      auto pv = [&](int m, int i) {  // O_m (+)= P_m V(i), P_m in tensor memory over S_m
+        const uint32_t vb = vd_base + (i & 1) * kTileBytes;
+#pragma unroll
+        for (int s = 0; s < kKT / 16; ++s) {
+          const uint64_t bd = tc::sdesc_sw128(vb + s * 2048, kHalf, 1024);
+          tc::mma_ts(tmem + 256 + m * 128, tmem + m * 128 + s * 8, bd, id_o,
+                     (i > 0 || s > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&o_done[m]);
+      };
+      if (ntiles > 0) {
+        ok = mbar_wait(&k_full[0], 0, a.status, 40);
+        if (ok) {
+          tc::fence_after_sync();
+          for (int m = 0; m < MT; ++m) qk(m, 0);
+          tc::mma_commit(&k_free[0]);
+        }
+      }
+      for (int i = 0; i < ntiles && ok; ++i) {
+        const bool more = i + 1 < ntiles;
+        ok = mbar_wait(&v_full[i & 1], (i >> 1) & 1, a.status, 41);
         for (int m = 0; m < MT && ok; ++m) {
-          ok = mbar_wait(&p_full[m][pb], (jj >> 1) & 1, a.status, 41);
+          ok = mbar_wait(&p_full[m], i & 1, a.status, 42);
           if (!ok) break;
           tc::fence_after_sync();
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const uint64_t bd = tc::sdesc_sw128(vd_base + vb * 16384 + s * 2048, 8192, 1024);
-            tc::mma_ts(tmem + 256 + m * 128, tmem + m * 128 + pb * 64 + s * 8, bd, id_o,
-                       (jj > 0 || s > 0) ? 1u : 0u);
+          pv(m, i);
+          if (more) {
+            if (m == 0) {
+              ok = mbar_wait(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, a.status, 43);
+              if (!ok) break;
+              tc::fence_after_sync();
+            }
+            qk(m, i + 1);  // S_m is free: P_m(i) is read by the PV issued just before
           }
-          tc::mma_commit(&o_done[m]);
         }
-        tc::mma_commit(&kv_empty[vb]);
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int buf = j % kKvBufs, sb = j & 1;
-        ok = mbar_wait(&kv_full[buf], (j / kKvBufs) & 1, a.status, 42);
         if (!ok) break;
-        tc::fence_after_sync();
-        for (int m = 0; m < MT; ++m) {
-#pragma unroll
-          for (int s = 0; s < 8; ++s) {
-            const uint64_t ad =
-                tc::sdesc_sw128(q_base + m * 32768 + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
-            const uint64_t bd =
-                tc::sdesc_sw128(kd_base + buf * 16384 + (s >> 2) * 8192 + (s & 3) * 32, 16, 1024);
-            tc::mma_ss(tmem + m * 128 + sb * 64, ad, bd, id_s, s > 0 ? 1u : 0u);
-          }
-          tc::mma_commit(&s_full[m][sb]);
-        }
-        if (j > 0) issue_pv(j - 1);
+        tc::mma_commit(&v_free[i & 1]);
+        if (more) tc::mma_commit(&k_free[(i + 1) & 1]);
       }
-      if (ok && ntiles > 0) issue_pv(ntiles - 1);
       tc::mma_commit(&mma_fin);
-      mbar_wait(&mma_fin, 0, a.status, 43);
+      mbar_wait(&mma_fin, 0, a.status, 44);
     }
   } else if (warp >= 4 && warp < 4 + 4 * MT) {
     // ---------------------------------------------------------------- softmax
@@ -363,32 +348,32 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     int lim = causal ? n - a.S + t : n - 1;
     lim = min(lim, k_stop - 1);
     const float c = a.scale * 1.4426950408889634f;
+    const uint32_t ts = tmem + lane_off + m * 128;
+    const uint32_t to = tmem + lane_off + 256 + m * 128;
     float m_run = kNegInfTc, l_run = 0.f;
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      ok = mbar_wait(&s_full[m][sb], (j >> 1) & 1, a.status, 44);
+    uint32_t x[32];
+    for (int i = 0; i < ntiles; ++i) {
+      ok = mbar_wait(&s_full[m], i & 1, a.status, 45);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc::fence_after_sync();
-      const uint32_t ts = tmem + lane_off + m * 128 + sb * 64;
-      uint32_t x[32], y[32];
-      tc::ld32(ts, x);
-      tc::ld32(ts + 32, y);
-      tc::wait_ld();
-      const int kbase = k_begin + j * kKT;
-      if (kbase + kKT - 1 > lim) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (kbase + i > lim) x[i] = __float_as_uint(kNegInfTc);
-          if (kbase + 32 + i > lim) y[i] = __float_as_uint(kNegInfTc);
-        }
-      }
-      // row max: eight independent chains, then a tree
+      const int kbase = k_begin + i * kKT;
+      const bool msk = kbase + kKT - 1 > lim;
+      // pass 1: row max, eight independent chains
       float mxa[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mxa[i] = fmaxf(__uint_as_float(x[i]), __uint_as_float(y[i]));
+      for (int e = 0; e < 8; ++e) mxa[e] = kNegInfTc;
+#pragma unroll 1
+      for (int ch = 0; ch < kKT / 32; ++ch) {
+        tc::ld32(ts + ch * 32, x);
+        tc::wait_ld();
+        if (msk) {
 #pragma unroll
-      for (int i = 8; i < 32; ++i)
-        mxa[i & 7] = fmaxf(mxa[i & 7], fmaxf(__uint_as_float(x[i]), __uint_as_float(y[i])));
+          for (int e = 0; e < 32; ++e)
+            if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(x[e]));
+      }
       const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                              fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       const float m_cand = mx * c;
@@ -399,71 +384,79 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         m_run = m_cand;
       }
       const float mu = m_run == kNegInfTc ? 0.f : m_run;
-      // p = 2^(s*c - mu) on the MUFU (or, with kPolyEvery > 0, partly by the polynomial)
+      // pass 2: p = 2^(s*c - mu) (MUFU, or partly the FMA-pipe polynomial), P over S.
+      // P chunk ch lands in columns [16ch, 16ch+16), all read already by chunks <= ch.
       float sa[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];
+#pragma unroll 1
+      for (int ch = 0; ch < kKT / 32; ++ch) {
+        tc::ld32(ts + ch * 32, x);
+        tc::wait_ld();
+        if (msk) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint32_t* src = i < 16 ? x : y;
-        const int e = (i & 15) * 2;
-        const float t0 = fmaf(__uint_as_float(src[e]), c, -mu);
-        const float t1 = fmaf(__uint_as_float(src[e + 1]), c, -mu);
-        const float p0 = (kPolyEvery > 0 && (2 * i) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(t0) : ex2(t0);
-        const float p1 = (kPolyEvery > 0 && (2 * i + 1) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(t1) : ex2(t1);
-        sa[(2 * i) & 3] += p0;
-        sa[(2 * i + 1) & 3] += p1;
-        pk[i] = PK::pack(p0, p1);
+          for (int e = 0; e < 32; ++e)
+            if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float u0 = fmaf(__uint_as_float(x[2 * e]), c, -mu);
+          const float u1 = fmaf(__uint_as_float(x[2 * e + 1]), c, -mu);
+          const float p0 =
+              (kPolyEvery > 0 && (2 * e) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(u0) : ex2(u0);
+          const float p1 = (kPolyEvery > 0 && (2 * e + 1) % kPolyEvery == kPolyEvery - 1)
+                               ? exp2_poly(u1)
+                               : ex2(u1);
+          sa[(2 * e) & 3] += p0;
+          sa[(2 * e + 1) & 3] += p1;
+          pk[e] = PK::pack(p0, p1);
+        }
+        tc::st16(ts + ch * 16, pk);
       }
-      const float sum = (sa[0] + sa[1]) + (sa[2] + sa[3]);
-      l_run = fmaf(l_run, alpha, sum);
-      tc::st32(ts, pk);  // P (16-bit pairs) over the first 32 columns of S
       tc::wait_st();
-      if (j > 0) {
-        // Wait for PV(j-1) on every tile: a parity wait only tells phases apart while the
+      l_run = fmaf(l_run, alpha, (sa[0] + sa[1]) + (sa[2] + sa[3]));
+      if (i > 0) {
+        // Wait for PV(i-1) on every tile: a parity wait only tells phases apart while the
         // barrier is at most one phase ahead of this thread's view of it, and a rescale
-        // needs O out of flight anyway. PV(j-1) normally finished during this softmax.
-        ok = mbar_wait(&o_done[m], (j - 1) & 1, a.status, 45);
+        // needs O out of flight anyway.
+        ok = mbar_wait(&o_done[m], (i - 1) & 1, a.status, 46);
         if (!__all_sync(0xffffffffu, ok)) break;
       }
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        // scale this row of O in place (PV(j) is not issued before p_full below)
+      if (i > 0 && __any_sync(0xffffffffu, resc)) {
+        // scale this row of O in place (PV(i) is not issued before p_full below)
         tc::fence_after_sync();
-        const uint32_t to = tmem + lane_off + 256 + m * 128;
 #pragma unroll 1
         for (int qd = 0; qd < 4; ++qd) {
           tc::ld32(to + qd * 32, x);
           tc::wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = __float_as_uint(__uint_as_float(x[i]) * alpha);
+          for (int e = 0; e < 32; ++e) x[e] = __float_as_uint(__uint_as_float(x[e]) * alpha);
           tc::st32(to + qd * 32, x);
         }
         tc::wait_st();
       }
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[m][sb]);
+      if (lane == 0) mbar_arrive(&p_full[m]);
     }
     // ---- epilogue: O row -> output (normalized) or partial row ---------------------------
     if (ok && ntiles > 0) {
-      ok = mbar_wait(&o_done[m], (ntiles - 1) & 1, a.status, 46);
+      ok = mbar_wait(&o_done[m], (ntiles - 1) & 1, a.status, 47);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc::fence_after_sync();
-      const uint32_t to = tmem + lane_off + 256 + m * 128;
       const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
       for (int qd = 0; qd < 4; ++qd) {
-        uint32_t x[32];
         if (ntiles > 0) {
           tc::ld32(to + qd * 32, x);
           tc::wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = 0u;
+          for (int e = 0; e < 32; ++e) x[e] = 0u;
         }
-        // column position p of 8-dim group holds dim perm[p] (4-bit) or p (8-bit)
+        // column position p of an 8-dim group holds dim perm[p] (4-bit) or p (8-bit)
         float o[32];
 #pragma unroll
         for (int g = 0; g < 4; ++g)
@@ -476,15 +469,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           if (P.parts) {
             float* dst = P.parts + ((long long)split * a.B * a.HQ * a.S + row) * (kD + 4) + qd * 32;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
           } else {
-            uint32_t* dst = reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(a.out) + row * kD + qd * 32);
+            uint32_t* dst =
+                reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(a.out) + row * kD + qd * 32);
 #pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(dst + i / 2) =
-                  make_uint4(PK::pack(o[i] * inv, o[i + 1] * inv), PK::pack(o[i + 2] * inv, o[i + 3] * inv),
-                             PK::pack(o[i + 4] * inv, o[i + 5] * inv), PK::pack(o[i + 6] * inv, o[i + 7] * inv));
+            for (int e = 0; e < 32; e += 8)
+              *reinterpret_cast<uint4*>(dst + e / 2) =
+                  make_uint4(PK::pack(o[e] * inv, o[e + 1] * inv), PK::pack(o[e + 2] * inv, o[e + 3] * inv),
+                             PK::pack(o[e + 4] * inv, o[e + 5] * inv), PK::pack(o[e + 6] * inv, o[e + 7] * inv));
           }
         }
       }
@@ -493,57 +487,67 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         *reinterpret_cast<float4*>(dst) = make_float4(m_run, l_run, 0.f, 0.f);
       }
     }
-  } else if (warp == 2 || warp == 3 || warp == 12 || warp == 13) {
+  } else if (warp == 1 || warp == 2 || warp == 3 || warp == 12) {
     // ---------------------------------------------------------------- dequantizers
-    const int dq = (warp < 4 ? warp - 2 : warp - 10) * 32 + lane;  // 0..127
-    const bool is_v = dq >= 64;
-    const int row = dq & 63;
-    uint8_t* dst_base = smem + (is_v ? SM::VD : SM::KD);
-    for (int j = 0; j < ntiles; ++j) {
-      const int st = j % GE::NST, buf = j % kKvBufs;
-      ok = mbar_wait(&code_full[st], (j / GE::NST) & 1, a.status, 47);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      const uint8_t* sp = smem + SM::RING + st * GE::STAGE;
-      const uint8_t* cp = sp + (is_v ? GE::CODE : 0);
-      uint32_t words[GE::RB / 4];
-#pragma unroll
-      for (int ch = 0; ch < GE::RB / 16; ++ch) {
-        const int sw = BITS == 4 ? ((ch ^ ((row >> 1) & 3)) & 3) : (ch ^ (row & 7));
-        const uint4 v = *reinterpret_cast<const uint4*>(cp + row * GE::RB + sw * 16);
-        words[4 * ch] = v.x;
-        words[4 * ch + 1] = v.y;
-        words[4 * ch + 2] = v.z;
-        words[4 * ch + 3] = v.w;
-      }
-      const uint32_t sc = *reinterpret_cast<const uint32_t*>(sp + 2 * GE::CODE + (is_v ? 2 : 0) * GE::SC + row * 4);
-      const uint32_t bi = *reinterpret_cast<const uint32_t*>(sp + 2 * GE::CODE + (is_v ? 3 : 1) * GE::SC + row * 4);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&code_empty[st]);
-      const uint32_t s0 = prmt(sc, 0u, 0x1010), s1 = prmt(sc, 0u, 0x3232);
-      const uint32_t b0 = prmt(bi, 0u, 0x1010), b1 = prmt(bi, 0u, 0x3232);
-      if (j >= kKvBufs) {  // PV(j - kKvBufs) released this buffer
-        ok = mbar_wait(&kv_empty[buf], ((j / kKvBufs) + 1) & 1, a.status, 48);
-        if (!__all_sync(0xffffffffu, ok)) break;
-      }
-      uint8_t* dst = dst_base + buf * 16384;
-      const int key = k_begin + j * kKT + row;
+    const int row = (warp == 12 ? 3 : warp - 1) * 32 + lane;  // key row of each tile, 0..127
+    const uint8_t* kw_base = reinterpret_cast<const uint8_t*>(a.kw) + (long long)bh * a.NP * RB;
+    const uint8_t* vw_base = reinterpret_cast<const uint8_t*>(a.vw) + (long long)bh * a.NP * RB;
+    const long long sc0 = (long long)bh * a.NP * 4;  // 2 groups x 16 bit per key
+    uint32_t kc[RW], vc[RW], ksc = 0, kbi = 0, vsc = 0, vbi = 0;
+    auto load = [&](int i) {  // codes and scales of key row `row` of tile i
+      const int key = k_begin + i * kKT + row;
       if (key < n) {
-        dequant_row<T, BITS>(words, s0, s1, b0, b1, dst, row);
+#pragma unroll
+        for (int u = 0; u < RW / 4; ++u) {
+          const uint4 kv = ldg16(kw_base + (long long)key * RB + u * 16);
+          const uint4 vv = ldg16(vw_base + (long long)key * RB + u * 16);
+          kc[4 * u] = kv.x; kc[4 * u + 1] = kv.y; kc[4 * u + 2] = kv.z; kc[4 * u + 3] = kv.w;
+          vc[4 * u] = vv.x; vc[4 * u + 1] = vv.y; vc[4 * u + 2] = vv.z; vc[4 * u + 3] = vv.w;
+        }
+        ksc = ldg4((const uint8_t*)a.ks + sc0 + (long long)key * 4);
+        kbi = ldg4((const uint8_t*)a.kb + sc0 + (long long)key * 4);
+        vsc = ldg4((const uint8_t*)a.vs + sc0 + (long long)key * 4);
+        vbi = ldg4((const uint8_t*)a.vb + sc0 + (long long)key * 4);
+      }
+    };
+    auto store = [&](const uint32_t* codes, uint32_t sc, uint32_t bi, bool valid, uint8_t* dst) {
+      if (valid) {
+        dequant_row<T, BITS>(codes, prmt(sc, 0u, 0x1010), prmt(sc, 0u, 0x3232),
+                             prmt(bi, 0u, 0x1010), prmt(bi, 0u, 0x3232), dst, row);
       } else {  // past the cache's valid length: zeros, so that P = 0 meets finite V
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          *reinterpret_cast<uint4*>(dst + (i >> 3) * 8192 + row * 128 + (((i & 7) ^ (row & 7)) * 16)) =
+        for (int e = 0; e < 16; ++e)
+          *reinterpret_cast<uint4*>(dst + (e >> 3) * kHalf + row * 128 + (((e & 7) ^ (row & 7)) * 16)) =
               make_uint4(0, 0, 0, 0);
       }
+    };
+    if (ntiles > 0) load(0);
+    for (int i = 0; i < ntiles; ++i) {
+      const int buf = i & 1;
+      const bool valid = k_begin + i * kKT + row < n;
+      if (i >= 2) {  // QK(i-2) released this K buffer
+        ok = mbar_wait(&k_free[buf], ((i >> 1) + 1) & 1, a.status, 48);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      store(kc, ksc, kbi, valid, smem + SM::KD + buf * kTileBytes);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&kv_full[buf]);
+      if (lane == 0) mbar_arrive(&k_full[buf]);
+      if (i >= 2) {  // PV(i-2) released this V buffer
+        ok = mbar_wait(&v_free[buf], ((i >> 1) + 1) & 1, a.status, 49);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      store(vc, vsc, vbi, valid, smem + SM::VD + buf * kTileBytes);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&v_full[buf]);
+      if (i + 1 < ntiles) load(i + 1);
     }
   }
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -551,17 +555,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
 
 template <typename T, int BITS, int MT>
 int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {
-  using SM = TcSmem<BITS, MT>;
+  using SM = TcSmem<MT>;
   TcParams prm;
   prm.a = a;
   prm.TT = p.tokens_per_tile;
   prm.chunk = p.chunk;
   const bool direct = combine && p.splits == 1 && a.out_kind == QKV_OUT_NORMALIZED;
   prm.parts = direct ? nullptr : reinterpret_cast<float*>(a.workspace);
-  constexpr int RB = kD * BITS / 8;
-  if (!make_code_map_bytes(&prm.tmk, a.kw, RB, a.NP, (long long)a.B * a.HKV, RB, kKT) ||
-      !make_code_map_bytes(&prm.tmv, a.vw, RB, a.NP, (long long)a.B * a.HKV, RB, kKT))
-    return QKV_ECUDA;
   const size_t smem = (size_t)SM::BYTES + 1024;
   auto kern = prefill_tc_kernel<T, BITS, MT>;
   static unsigned attr_done = 0;
