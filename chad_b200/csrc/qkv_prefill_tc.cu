@@ -46,7 +46,7 @@ constexpr int kKT = 128;         // keys per tile (MMA N of Q K^T)
 constexpr int kWarpsTc = 13;
 constexpr int kThreadsTc = kWarpsTc * 32;
 constexpr float kRescaleLog2 = 8.0f;
-constexpr int kPolyEvery = 0;  // > 0: one exp2 in kPolyEvery on the FMA pipe, not the MUFU
+constexpr int kPolyPairs = 4;  // > 0: one value pair in kPolyPairs takes exp2_poly2, not the MUFU
 constexpr int kHalf = kKT * 128;       // bytes of one 64-dim half of a K or V tile
 constexpr int kTileBytes = 2 * kHalf;  // one dequantized K or V tile
 #define kNegInfTc (-__int_as_float(0x7f800000))
@@ -115,15 +115,42 @@ struct Pack16<__half> {
   }
 };
 
-// 2^t on the FMA/ALU pipes: t = n + f with n = rint(t), |f| <= 1/2; 2^f from a degree-3
-// polynomial fitted here to relative error 8e-5 over [-1/2, 1/2] (far below the 16-bit P it
-// feeds), 2^n added to the exponent bits. t is clamped at -126: 2^-126 stands in for 0.
-__device__ __forceinline__ float exp2_poly(float t) {
-  t = fmaxf(t, -126.0f);
-  const float j = t + 12582912.0f;        // 1.5 * 2^23: low mantissa bits hold rint(t)
-  const float f = t - (j - 12582912.0f);
-  const float p = fmaf(fmaf(fmaf(0.05518098f, f, 0.24263459f), f, 0.69326133f), f, 0.99992621f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+// Packed fp32 pair arithmetic (sm_100): two lanes of work per issued instruction.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                     float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^t for a pair of values on the FMA/ALU pipes instead of the MUFU: t = n + f with
+// n = rint(t), |f| <= 1/2; 2^f from a degree-3 polynomial fitted here to relative error 8e-5
+// over [-1/2, 1/2] (far below the 16-bit P it feeds); 2^n enters the exponent bits through
+// one integer multiply-add per value. t is clamped at -126: 2^-126 stands in for 0.
+__device__ __forceinline__ void exp2_poly2(float& p0, float& p1, float t0, float t1) {
+  t0 = fmaxf(t0, -126.0f);
+  t1 = fmaxf(t1, -126.0f);
+  float j0, j1, n0, n1, f0, f1, q0, q1;
+  add2(j0, j1, t0, t1, 12582912.0f, 12582912.0f);  // 1.5 * 2^23: low mantissa bits = rint(t)
+  add2(n0, n1, j0, j1, -12582912.0f, -12582912.0f);
+  fma2(f0, f1, n0, n1, -1.0f, -1.0f, t0, t1);
+  fma2(q0, q1, 0.05518098f, 0.05518098f, f0, f1, 0.24263459f, 0.24263459f);
+  fma2(q0, q1, q0, q1, f0, f1, 0.69326133f, 0.69326133f);
+  fma2(q0, q1, q0, q1, f0, f1, 0.99992621f, 0.99992621f);
+  p0 = __uint_as_float(__float_as_uint(j0) * 8388608u + __float_as_uint(q0));
+  p1 = __uint_as_float(__float_as_uint(j1) * 8388608u + __float_as_uint(q1));
 }
 
 // code (exact, in T) pair -> round(code * s + b), one rounding, both halves
@@ -372,7 +399,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
             if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
         }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(x[e]));
+        for (int e = 0; e < 16; ++e)
+          mxa[e & 7] = max3(mxa[e & 7], __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
       }
       const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                              fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
@@ -384,7 +412,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         m_run = m_cand;
       }
       const float mu = m_run == kNegInfTc ? 0.f : m_run;
-      // pass 2: p = 2^(s*c - mu) (MUFU, or partly the FMA-pipe polynomial), P over S.
+      // pass 2: p = 2^(s*c - mu) (MUFU; one pair in kPolyPairs by the FMA-pipe polynomial),
+      // P over S.
       // P chunk ch lands in columns [16ch, 16ch+16), all read already by chunks <= ch.
       float sa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
@@ -399,15 +428,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float u0 = fmaf(__uint_as_float(x[2 * e]), c, -mu);
-          const float u1 = fmaf(__uint_as_float(x[2 * e + 1]), c, -mu);
-          const float p0 =
-              (kPolyEvery > 0 && (2 * e) % kPolyEvery == kPolyEvery - 1) ? exp2_poly(u0) : ex2(u0);
-          const float p1 = (kPolyEvery > 0 && (2 * e + 1) % kPolyEvery == kPolyEvery - 1)
-                               ? exp2_poly(u1)
-                               : ex2(u1);
-          sa[(2 * e) & 3] += p0;
-          sa[(2 * e + 1) & 3] += p1;
+          float u0, u1, p0, p1;
+          fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
+          if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
+            exp2_poly2(p0, p1, u0, u1);
+          } else {
+            p0 = ex2(u0);
+            p1 = ex2(u1);
+          }
+          add2(sa[2 * (e & 1)], sa[2 * (e & 1) + 1], sa[2 * (e & 1)], sa[2 * (e & 1) + 1], p0, p1);
           pk[e] = PK::pack(p0, p1);
         }
         tc::st16(ts + ch * 16, pk);
