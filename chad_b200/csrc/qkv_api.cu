@@ -239,7 +239,9 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
                 (long long)B * HKV * rg, kMaxCounters);
   decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
   size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
-  a.use_tc = prefill_tc_eligible(B, HQ, HKV, S, D, lens, pos_base, total_lens, a.mask_kind);
+  // (the tensor-core path's running max assumes a positive softmax scale)
+  a.use_tc = prefill_tc_eligible(B, HQ, HKV, S, D, lens, pos_base, total_lens, a.mask_kind) &&
+             scale > 0.f;
   if (a.use_tc) {
     a.tc = prefill_tc_plan(B, HQ, HKV, S, n_max, splits);
     need = prefill_tc_workspace_bytes(B, HQ, S, D, a.tc, direct);

@@ -385,61 +385,118 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       tc::fence_after_sync();
       const int kbase = k_begin + i * kKT;
       const bool msk = kbase + kKT - 1 > lim;
-      // pass 1: row max, eight independent chains
-      float mxa[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mxa[e] = kNegInfTc;
-#pragma unroll 1
-      for (int ch = 0; ch < kKT / 32; ++ch) {
-        tc::ld32(ts + ch * 32, x);
-        tc::wait_ld();
-        if (msk) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          mxa[e & 7] = max3(mxa[e & 7], __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                             fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      const float m_cand = mx * c;
-      float alpha = 1.f;
-      const bool resc = m_cand > m_run + kRescaleLog2;  // false while the tile is all masked
-      if (resc) {
-        alpha = ex2(m_run - m_cand);
-        m_run = m_cand;
-      }
-      const float mu = m_run == kNegInfTc ? 0.f : m_run;
-      // pass 2: p = 2^(s*c - mu) (MUFU; one pair in kPolyPairs by the FMA-pipe polynomial),
-      // P over S.
-      // P chunk ch lands in columns [16ch, 16ch+16), all read already by chunks <= ch.
+      // Fast path: one pass against the running max. Every chunk's max must stay within 2^8
+      // of it (one vote per chunk); P stays in registers until all chunks passed, so S is
+      // still intact for the two-pass path, which handles the first tile and a new maximum.
       float sa[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int ch = 0; ch < kKT / 32; ++ch) {
-        tc::ld32(ts + ch * 32, x);
-        tc::wait_ld();
-        if (msk) {
+      float alpha = 1.f;
+      bool resc = false;
+      bool fast = __all_sync(0xffffffffu, m_run != kNegInfTc);
+      if (fast) {
+        const float mu = m_run;
+        const float s_hi = (m_run + kRescaleLog2) / c;  // largest raw score the pass accepts
+        uint32_t pf[64];
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
-        }
-        uint32_t pk[16];
+        for (int ch = 0; ch < kKT / 32; ++ch) {
+          tc::ld32(ts + ch * 32, x);
+          tc::wait_ld();
+          if (msk) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float u0, u1, p0, p1;
-          fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
-          if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
-            exp2_poly2(p0, p1, u0, u1);
-          } else {
-            p0 = ex2(u0);
-            p1 = ex2(u1);
+            for (int e = 0; e < 32; ++e)
+              if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
           }
-          add2(sa[2 * (e & 1)], sa[2 * (e & 1) + 1], sa[2 * (e & 1)], sa[2 * (e & 1) + 1], p0, p1);
-          pk[e] = PK::pack(p0, p1);
+          float cm[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) cm[e] = fmaxf(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
+#pragma unroll
+          for (int e = 4; e < 16; ++e)
+            cm[e & 3] = max3(cm[e & 3], __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
+          if (__any_sync(0xffffffffu, fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])) > s_hi)) {
+            fast = false;
+            break;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float u0, u1, p0, p1;
+            fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
+            if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
+              exp2_poly2(p0, p1, u0, u1);
+            } else {
+              p0 = ex2(u0);
+              p1 = ex2(u1);
+            }
+            add2(sa[2 * (e & 1)], sa[2 * (e & 1) + 1], sa[2 * (e & 1)], sa[2 * (e & 1) + 1], p0, p1);
+            pf[ch * 16 + e] = PK::pack(p0, p1);
+          }
         }
-        tc::st16(ts + ch * 16, pk);
+        if (fast) {
+          uint32_t h0[32], h1[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            h0[e] = pf[e];
+            h1[e] = pf[32 + e];
+          }
+          tc::st32(ts, h0);
+          tc::st32(ts + 32, h1);
+        } else {
+          sa[0] = sa[1] = sa[2] = sa[3] = 0.f;
+        }
+      }
+      if (!fast) {
+        // pass 1: row max, eight independent chains
+        float mxa[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mxa[e] = kNegInfTc;
+#pragma unroll 1
+        for (int ch = 0; ch < kKT / 32; ++ch) {
+          tc::ld32(ts + ch * 32, x);
+          tc::wait_ld();
+          if (msk) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            mxa[e & 7] = max3(mxa[e & 7], __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                               fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+        const float m_cand = mx * c;
+        resc = m_cand > m_run + kRescaleLog2;  // false while the tile is all masked
+        if (resc) {
+          alpha = ex2(m_run - m_cand);
+          m_run = m_cand;
+        }
+        const float mu = m_run == kNegInfTc ? 0.f : m_run;
+        // pass 2: p = 2^(s*c - mu) (MUFU; one pair in kPolyPairs by the FMA-pipe polynomial),
+        // P over S.
+        // P chunk ch lands in columns [16ch, 16ch+16), all read already by chunks <= ch.
+#pragma unroll 1
+        for (int ch = 0; ch < kKT / 32; ++ch) {
+          tc::ld32(ts + ch * 32, x);
+          tc::wait_ld();
+          if (msk) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (kbase + ch * 32 + e > lim) x[e] = __float_as_uint(kNegInfTc);
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float u0, u1, p0, p1;
+            fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
+            if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
+              exp2_poly2(p0, p1, u0, u1);
+            } else {
+              p0 = ex2(u0);
+              p1 = ex2(u1);
+            }
+            add2(sa[2 * (e & 1)], sa[2 * (e & 1) + 1], sa[2 * (e & 1)], sa[2 * (e & 1) + 1], p0, p1);
+            pk[e] = PK::pack(p0, p1);
+          }
+          tc::st16(ts + ch * 16, pk);
+        }
       }
       tc::wait_st();
       l_run = fmaf(l_run, alpha, (sa[0] + sa[1]) + (sa[2] + sa[3]));
