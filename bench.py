@@ -2,7 +2,8 @@
 """Quantized-KV decode attention benchmark (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode32k-8bit|decode32k-4bit|longctx]
+                    [--workload decode32k-8bit|decode32k-4bit|longctx|
+                                verify16k-4bit|prefill32k-4bit]
 
 A step is one decode token through `--layers` (48) attention layers, each with its own
 quantized KV cache (inputs far larger than L2). The default workload is the 8-bit 32K
@@ -43,6 +44,15 @@ WORKLOADS = {
     # B4, ragged 64K-128K, 4-bit, sequence split across the GPUs
     "longctx": dict(B=4, HQ=32, HKV=4, D=128, N=131072, bits=4, ragged=True),
 }
+# multi-token workloads (one GPU; with N GPUs every rank runs an independent replica)
+CHUNK_WORKLOADS = {
+    # 8 draft tokens at the tail of a 16K 4-bit cache, causal in the block
+    "verify16k-4bit": dict(B=1, HQ=32, HKV=4, D=128, N=16384, S=8, bits=4, layers=48,
+                           ragged=False),
+    # 2048 new tokens after a 30720-token 4-bit prefix, causal in the chunk
+    "prefill32k-4bit": dict(B=1, HQ=32, HKV=4, D=128, N=30720 + 2048, S=2048, bits=4, layers=8,
+                            ragged=False),
+}
 METRIC = "qKV decode attn: HBM GB/s & µs/layer at 32K ctx; tok/s at 1/2/4/8 B200"
 OUTLIERS = (3, 37, 70, 101)
 
@@ -65,12 +75,208 @@ def load_traffic(workload):
     return None
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
+    fallback = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
+            return float(json.load(f)[key]), "measured"
     except Exception:  # noqa: BLE001
-        return 6650.0, "fallback"
+        return fallback[key], "fallback"
+
+
+def chunk_flops(cfg):
+    """Algorithmic FLOPs of one layer: QK^T and PV over the keys each query row sees."""
+    S, N, D, HQ, B = cfg["S"], cfg["N"], cfg["D"], cfg["HQ"], cfg["B"]
+    prefix = N - S
+    return 4.0 * D * HQ * B * (S * prefix + S * (S + 1) / 2)
+
+
+def run_chunk(args, cfg, rank, world, device):
+    """Multi-token attention (verify block / prefill chunk) over quantized caches: a step is
+    the S new tokens of one sequence through `layers` layers, each with its own cache."""
+    import torch.distributed as dist
+
+    from chad_b200 import ops
+
+    torch.cuda.set_device(device)
+    L = cfg["layers"]
+    B, HQ, HKV, D, S, N, bits = (cfg[k] for k in ("B", "HQ", "HKV", "D", "S", "N", "bits"))
+    prefill = S > 64
+    caches = build_layers(cfg, L, [N] * B, device, seed=rank + 1)
+    scale = D ** -0.5
+    gq = torch.Generator(device=device).manual_seed(11)
+    q = torch.randn((L, B, HQ, S, D), generator=gq, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws = torch.zeros(ops.workspace_size(B, HQ, HKV, S, D, N, bits), dtype=torch.uint8,
+                     device=device)
+
+    def layer_calls():
+        for l in range(L):
+            ops.attention(q[l], caches[l].keys, caches[l].values, scale, N, bits, mask="causal",
+                          out=out[l], workspace=ws)
+
+    stream = torch.cuda.Stream(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        layer_calls()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            layer_calls()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        ev0.record()  # graph replays go to the current stream
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # dominant kernel alone: prefill = the tensor-core kernel (one launch per layer when a
+    # single split covers the keys); verify = the split kernel without its combine
+    if prefill:
+        kern_us = ms * 1e3 / L
+        kern_name = "prefill_tc_kernel"
+    else:
+        parts_buf = torch.empty(ws.numel() // 4 + 1, dtype=torch.float32, device=device)
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for l in range(L):
+                ops.partials(q[l], caches[l].keys, caches[l].values, scale, N, bits,
+                             mask="causal", parts=parts_buf)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g2, stream=stream):
+                for l in range(L):
+                    ops.partials(q[l], caches[l].keys, caches[l].values, scale, N, bits,
+                                 mask="causal", parts=parts_buf)
+        for _ in range(3):
+            g2.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, min(50, args.steps))
+        e0.record()
+        for _ in range(reps):
+            g2.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        kern_us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+        kern_name = "decode_split_kernel"
+
+    # e2e: pinned host queries and new-token K/V in, quantize-append, attention, output out
+    hq = torch.empty((L, B, HQ, S, D), dtype=torch.bfloat16).pin_memory()
+    hq.copy_(q.cpu())
+    hk = torch.randn((L, B, HKV, S, D)).to(torch.bfloat16).pin_memory()
+    hv = torch.randn((L, B, HKV, S, D)).to(torch.bfloat16).pin_memory()
+    hout = torch.empty((L, B, HQ, S, D), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(q), hk.to(device), hv.to(device)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        for l in range(L):
+            out[l].copy_(ops.prefill(dq[l], dk[l], dv[l], caches[l].keys, caches[l].values,
+                                     N - S, bits, scale))
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 50))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    if rank != 0:
+        return None
+
+    flops_layer = chunk_flops(cfg)
+    kv_layer = B * N * HKV * kv_bytes_per_key(D, bits)
+    if prefill:
+        unit, per_layer = "TFLOP/s", flops_layer / 1e12
+        peak, peak_kind = measured_peak("bf16_tflops_sustained")
+        roof = {"bound": "tensor", "kernel": kern_name, "unit": "TFLOP/s",
+                "flops_per_launch": flops_layer}
+    else:
+        unit, per_layer = "GB/s", kv_layer / 1e9
+        peak, peak_kind = measured_peak("hbm_gbs")
+        roof = {"bound": "hbm", "kernel": kern_name, "unit": "GB/s",
+                "bytes_per_launch": kv_layer}
+    achieved = per_layer / (kern_us * 1e-6)
+    roof.update({"achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                 "frac": round(achieved / peak, 4), "launch_us": round(kern_us, 3),
+                 "traffic": None})
+    value = per_layer * L * world / (ms * 1e-3)
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "us_per_layer": round(ms * 1e3 / L, 3),
+        "tok_per_s": round(B * S * L / (ms * 1e-3) / L, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                   "head_dim": D, "new_tokens": S, "keys": N, "kv_bits": bits,
+                   "group_size": 64, "mask": "causal", "layers_per_step": L,
+                   "l2": f"inputs larger than L2: {L} distinct layer caches, "
+                         f"{kv_layer * L / 1e9:.2f} GB",
+                   "parallelism": f"{world} independent replicas" if world > 1 else "single GPU"},
+        "roofline": roof,
+        "e2e": {"value": round(per_layer * L * world / (e2e_ms * 1e-3), 2), "unit": unit,
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
+                "d2h_bytes_per_step": hout.numel() * 2},
+        "clocks": clocks.summary(),
+        "gpu_launches": (L if prefill else 2 * L) * args.steps,
+    }
+
+
+def cpu_sample_chunk(cfg, seconds=10.0):
+    """Reference path on the host cores for a multi-token workload: the first `s` query tokens
+    of one layer (at least one call, growing until ~`seconds`); returns (unit value, threads,
+    calls, seconds, tokens)."""
+    from oracle import cpu_stock
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, HQ, HKV, D, S, N, bits = (cfg[k] for k in ("B", "HQ", "HKV", "D", "S", "N", "bits"))
+    g = torch.Generator().manual_seed(3)
+    per = 32 // bits
+    kq = (torch.randint(-2**31, 2**31 - 1, (B, HKV, N, D // per), generator=g, dtype=torch.int64)
+          .to(torch.int32),
+          (torch.rand((B, HKV, N, D // 64), generator=g) * 0.1).to(torch.bfloat16),
+          torch.randn((B, HKV, N, D // 64), generator=g).to(torch.bfloat16))
+    vq = tuple(t.clone() for t in kq)
+    s = min(S, 64)
+    q = torch.randn((B, HQ, s, D), generator=g).to(torch.bfloat16)
+    pos0 = N - S
+    cpu_stock.attention(q, kq, vq, D ** -0.5, N, bits, causal=True, q_pos0=pos0)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        cpu_stock.attention(q, kq, vq, D ** -0.5, N, bits, causal=True, q_pos0=pos0)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    if S > 64:  # FLOPs of the sampled rows
+        work = 4.0 * D * HQ * B * s * (pos0 + (s + 1) / 2) / 1e12
+    else:  # the whole cache is read for the sampled block
+        work = B * N * HKV * kv_bytes_per_key(D, bits) / 1e9
+    return work * calls / el, torch.get_num_threads(), calls, el, s
 
 
 class ClockSampler:
@@ -449,6 +655,36 @@ def run_reference(args, cfg):
     }
 
 
+def run_reference_chunk(args, cfg):
+    """--impl reference for the multi-token workloads: per step, the reference path restated
+    on the host cores for the first query tokens of one layer (bounded sample)."""
+    steps = args.steps
+    v, cores, calls, el, s = cpu_sample_chunk(cfg, seconds=0.0)  # warm + one call
+    t0 = time.perf_counter()
+    v_sum = 0.0
+    for _ in range(steps):
+        vi, cores, calls, eli, s = cpu_sample_chunk(cfg, seconds=0.0)
+        v_sum += vi
+    el = time.perf_counter() - t0
+    value = v_sum / steps
+    unit = "TFLOP/s" if cfg["S"] > 64 else "GB/s"
+    sample = (f"the first {s} query tokens of one layer ({cfg['N']} keys, {cfg['bits']}-bit) "
+              f"per step, torch-CPU fp32")
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": unit,
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "batch": cfg["B"], "q_heads": cfg["HQ"],
+                   "kv_heads": cfg["HKV"], "head_dim": cfg["D"], "new_tokens": cfg["S"],
+                   "keys": cfg["N"], "kv_bits": cfg["bits"], "group_size": 64},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -456,11 +692,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode32k-8bit")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(CHUNK_WORKLOADS),
+                    default="decode32k-8bit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = WORKLOADS[args.workload]
+    cfg = WORKLOADS.get(args.workload) or CHUNK_WORKLOADS[args.workload]
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -468,7 +705,10 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args, cfg)), flush=True)
+            if args.workload in CHUNK_WORKLOADS:
+                print(json.dumps(run_reference_chunk(args, cfg)), flush=True)
+            else:
+                print(json.dumps(run_reference(args, cfg)), flush=True)
         return
 
     import datetime
@@ -481,6 +721,18 @@ def main():
                                 device_id=torch.device("cuda", local))
     device = f"cuda:{local}"
     try:
+        if args.workload in CHUNK_WORKLOADS:
+            res = run_chunk(args, cfg, rank, world, device)
+            if rank == 0 and res is not None and world == 1:
+                v, cores, calls, el, s = cpu_sample_chunk(cfg, args.cpu_seconds)
+                res["cpu_baseline"] = {
+                    "value": round(v, 4), "unit": res["unit"], "cores": cores, "kind": "port",
+                    "sample": f"{calls} calls of the first {s} query tokens of one layer "
+                              f"through the reference path restated in torch-CPU fp32, "
+                              f"{el:.1f} s"}
+            if rank == 0 and res is not None:
+                print(json.dumps(res), flush=True)
+            return
         res = run_ours(args, cfg, rank, world, device)
         if rank == 0 and res is not None:
             if world == 1:

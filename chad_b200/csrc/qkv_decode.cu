@@ -70,7 +70,7 @@ template <int BITS, int D, int NT>
 struct DecodeCfg {
   static constexpr bool kNarrow = NT == 1 && D <= 128;
   static constexpr int SUB = kNarrow && BITS == 4 ? 2 : 1;
-  static constexpr int CTAS = kNarrow ? 3 : 2;
+  static constexpr int CTAS = kNarrow && BITS == 8 ? 3 : 2;
   static constexpr int TP = 64 * SUB;  // keys per stage
   static constexpr int RING = CTAS == 3 ? 64 * 1024 : 104 * 1024;
 };
@@ -406,6 +406,8 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     const int v0k = key_perm<BITS>(2 * tq), v1k = key_perm<BITS>(2 * tq + 1);
     const int v2k = key_perm<BITS>(2 * tq + 8), v3k = key_perm<BITS>(2 * tq + 9);
     const bool any_mask = a.mask_kind != QKV_MASK_NONE;
+    const bool causal = a.mask_kind == QKV_MASK_CAUSAL;
+    const bool array_mask = any_mask && !causal;
     const int pb = a.pos_base ? a.pos_base[b] : 0;
     const int tot = a.total_lens ? a.total_lens[b] : len;
 
@@ -492,8 +494,9 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
             }
         }
 
-        // ---- masking (only tiles that need it) ----------------------------------------
-        if (tail || any_mask) {
+        // ---- masking (only tiles that need it: a causal mask hides nothing before the
+        // first query row's position) ----------------------------------------------------
+        if (tail || array_mask || (causal && pb + p0 + 16 * kSub - 1 > tot - a.S)) {
 #pragma unroll
           for (int h = 0; h < kSub; ++h)
 #pragma unroll
@@ -1069,7 +1072,7 @@ void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int 
   const int cls[4] = {1, 2, 4, 8};
   for (int i = 0; i < 4; ++i) {
     int mc = max_clusters_any(bits, D, R, cls[i]);
-    if (mc <= 0) mc = (i == 0 ? 1 : 0) * (decode_ctas_per_sm(R, D) * num_sms());  // no query
+    if (mc <= 0) mc = (i == 0 ? 1 : 0) * (decode_ctas_per_sm(R, D, bits) * num_sms());  // no query
     ctas[i] = mc * cls[i];
     if (ctas[i] > best_ctas) best_ctas = ctas[i];
   }

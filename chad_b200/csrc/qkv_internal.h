@@ -61,7 +61,9 @@ size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluste
 void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want_splits,
                  int* splits, int* chunk, int* cluster);
 // resident CTAs per SM the decode kernel is built for (register budget per instantiation)
-inline int decode_ctas_per_sm(int R, int D) { return (R <= 8 && D <= 128) ? 3 : 2; }
+inline int decode_ctas_per_sm(int R, int D, int bits) {
+  return (R <= 8 && D <= 128 && bits == 8) ? 3 : 2;
+}
 
 int launch_decode(const AttnArgs& a, cudaStream_t st);  // split kernel + combine
 int launch_split_only(const AttnArgs& a, cudaStream_t st);  // partial rows into a.workspace

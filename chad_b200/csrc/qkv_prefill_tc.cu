@@ -682,7 +682,7 @@ bool prefill_tc_eligible(int B, int HQ, int HKV, int S, int D, const int* lens,
   const int gqa = HQ / HKV;
   if (gqa > 128 || 128 % gqa) return false;
   (void)B;
-  return gqa * S >= 128;  // at least one full MMA tile of query rows
+  return gqa * S >= 64;  // at least half a 128-row MMA tile of query rows
 }
 
 TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits) {
@@ -697,11 +697,13 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
   int best = 1;
   if (want_splits > 0) {
     best = want_splits;
+  } else if (units >= sms) {
+    best = 1;  // a full wave without splitting: split partials would only add traffic
   } else {
-    // fewest splits that fill the waves to >= 90 %, keeping >= 512 keys per split
+    // fewest splits that fill the waves to >= 90 %, keeping >= 256 keys per split
     double best_eff = 0.0;
-    for (int s = 1; s <= 16; ++s) {
-      if (s > 1 && (n + s - 1) / s < 512) break;
+    for (int s = 1; s <= 64; ++s) {
+      if (s > 1 && (n + s - 1) / s < 256) break;
       const long long ctas = (long long)units * s;
       const long long waves = (ctas + sms - 1) / sms;
       const double eff = (double)ctas / (double)(waves * sms);

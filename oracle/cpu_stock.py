@@ -28,13 +28,19 @@ def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits
 
 
 def attention(q: torch.Tensor, kq, vq, scale: float, n: int, bits: int,
-              group_size: int = 64) -> torch.Tensor:
-    """q (B, HQ, S, D) CPU; kq/vq (w, scales, biases) CPU with >= n positions."""
+              group_size: int = 64, causal: bool = False, q_pos0=None) -> torch.Tensor:
+    """q (B, HQ, S, D) CPU; kq/vq (w, scales, biases) CPU with >= n positions.
+
+    causal: query s sits at key position q_pos0 + s (default n - S, the cache tail) and sees
+    the keys up to it, as in the reference's causal multi-token branch."""
     k = dequantize(*(t[:, :, :n] for t in kq), bits, group_size).float()
     v = dequantize(*(t[:, :, :n] for t in vq), bits, group_size).float()
     b, hq, s, d = q.shape
     hkv = k.shape[1]
     qf = (q.float() * scale).view(b, hkv, hq // hkv, s, d)
     sc = qf @ k.unsqueeze(2).transpose(-1, -2)
+    if causal:
+        pos = torch.arange(s).unsqueeze(1) + (n - s if q_pos0 is None else q_pos0)
+        sc = sc.masked_fill(torch.arange(n).unsqueeze(0) > pos, float("-inf"))
     p = torch.softmax(sc, dim=-1)
     return (p @ v.unsqueeze(2)).view(b, hq, s, d).to(q.dtype)

@@ -165,6 +165,14 @@ def test_multi_token_causal(S, bits):
     _attn_check(q, k, v, bits, "bf16", n, 2e-2, 2e-3, mask="causal")
 
 
+@pytest.mark.parametrize("S,n", [(8, 1000), (5, 3000), (16, 130)])
+def test_multi_token_causal_row_groups(S, n):
+    """GQA 4: 4*S query rows per kv head stay on the split-KV kernel, whose causal mask is
+    only evaluated on tiles past the first draft position."""
+    q, k, v = make_case(40 + S, 1, 16, 4, S, 128, n, "bf16", outliers=True)
+    _attn_check(q, k, v, 4, "bf16", n, 2e-2, 2e-3, mask="causal")
+
+
 def test_bool_and_additive_masks():
     n = 500
     q, k, v = make_case(21, 1, 16, 2, 2, 128, n, "bf16")

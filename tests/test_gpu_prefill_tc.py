@@ -1,6 +1,6 @@
 """Tensor-core multi-token path (tcgen05) vs the CPU oracle, through the C ABI.
 
-Calls with head_dim 128, a GQA group dividing 128, at least 128 query rows per kv head and
+Calls with head_dim 128, a GQA group dividing 128, at least 64 query rows per kv head and
 no mask or a causal mask take the tcgen05 kernel (qkv_prefill_tc.cu). Like the reference's
 multi-token branch (src/chad/mlx_qsdpa.py:751-766) it attends over K/V dequantized to the
 query dtype, so it is held to the configurations' tolerance (max-abs 2e-2, mean-abs 2e-3)
@@ -139,3 +139,13 @@ def test_repeated_calls_are_bit_identical():
     first = _run(q, c, n, 4, "bf16", "causal", splits=1)
     for _ in range(6):
         assert torch.equal(first, _run(q, c, n, 4, "bf16", "causal", splits=1))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_verify_block_shape(bits):
+    """A speculative-verify block (8 draft tokens at the cache tail, GQA 8: 64 query rows per
+    kv head, half a tile) split over many key ranges."""
+    S, n = 8, 6000 + 8
+    q, k, v = make_case(70 + bits, 1, 32, 4, S, 128, n, "bf16", outliers=True)
+    c = _cache(k, v, bits, "bf16")
+    _check(_run(q, c, n, bits, "bf16", "causal"), _ref(q, k, v, bits, "bf16", n, "causal"))
