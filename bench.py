@@ -62,13 +62,14 @@ def kv_bytes_per_key(D, bits):
     return 2 * (D * bits // 8 + 2 * (D // 64) * 2)
 
 
-def load_traffic(workload):
-    """DRAM bytes per launch of the split kernel from a committed ncu summary, if any."""
+def load_traffic(workload, kernel="decode_split"):
+    """DRAM bytes per launch of the workload's dominant kernel from a committed ncu summary
+    (profiles/traffic.txt: workload, kernel tag, bytes), if any."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
     try:
         for line in open(path):
             parts = line.split()
-            if len(parts) >= 3 and parts[0] == workload and parts[1] == "decode_split":
+            if len(parts) >= 3 and parts[0] == workload and parts[1] == kernel:
                 return float(parts[2])
     except OSError:
         pass
@@ -221,7 +222,8 @@ def run_chunk(args, cfg, rank, world, device):
     achieved = per_layer / (kern_us * 1e-6)
     roof.update({"achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
                  "frac": round(achieved / peak, 4), "launch_us": round(kern_us, 3),
-                 "traffic": None})
+                 "traffic": load_traffic(args.workload,
+                                         "prefill_tc" if prefill else "decode_split")})
     value = per_layer * L * world / (ms * 1e-3)
     return {
         "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world,
