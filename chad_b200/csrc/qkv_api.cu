@@ -10,6 +10,8 @@
 #include "../../include/qkv.h"
 #include "qkv_internal.h"
 
+static_assert(qkv::kCounterBytes == QKV_COUNTER_BYTES, "counter area size");
+
 namespace qkv {
 
 __device__ int g_device_status = 0;

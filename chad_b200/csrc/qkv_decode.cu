@@ -45,8 +45,8 @@ namespace {
 constexpr int kWarps = 4;                    // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kBoxRows = 64;                 // key rows per TMA box
-constexpr int kMaxCluster = 8;
-constexpr int kMaxClustersPerGroup = 64;  // bounds the final merge's shared-memory tables
+constexpr int kMergeSlots = kThreads / 16;  // partial subsets merged side by side per unit
+constexpr int kMaxSplits = 256;              // bounds the merge's loads per thread
 #define kNegInf (-__int_as_float(0x7f800000))
 
 // Order in which the 16 keys of a warp tile occupy the MMA rows. The tables make the rows
@@ -155,24 +155,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ float ld_dsmem_f32(const void* local, uint32_t cta) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(cta));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+
 
 // Position of output element (query row r, head dim d) in the MMA fragment order the
 // consumer warps publish their accumulators in.
@@ -188,8 +181,9 @@ struct DecodeParams {
   AttnArgs a;
   CUtensorMap tmk;  // K codes: (RB bytes, NP, B*HKV)
   CUtensorMap tmv;  // V codes
-  float* gpart;     // cluster partials [clusters][B*HQ*S][D+4]
-  int clusters;     // clusters per (b, kv head, row group) = splits / cluster size
+  float* gpart;     // per-CTA partial rows [splits][B*HQ*S][D+4]
+  int* counters;    // [2][kMaxCounters] arrivals and finished mergers per row group
+  int merge;        // 1: the row group's last CTAs merge the partials into a.out
 };
 
 template <typename T, int BITS, int D, int NT>
@@ -221,9 +215,6 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;  // MMA group id
   const int tq = lane & 3;   // thread in group
-  const uint32_t crank = cluster_rank();
-  const int csize = a.cluster;       // CTAs per cluster
-  const int cidx = split / csize;    // cluster index within the row group
 
   const int gqa = a.HQ / a.HKV;
   const int R = gqa * a.S;  // query rows sharing this kv head
@@ -295,10 +286,9 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   float* cp = ow + kWarps * RG * D;            // [RG*D] this CTA's output, fragment order
   float* cm = cp + RG * D;                     // [RG] this CTA's max per row
   float* cl = cm + RG;                         // [RG] this CTA's sum per row
-  float* tm = cl + RG;                         // [kMaxCluster][RG] cluster members' max
-  float* tl = tm + kMaxCluster * RG;           // [kMaxCluster][RG] their sums
-  float* tf = tl + kMaxCluster * RG;           // [kMaxCluster][RG] their weights
-  float* ml = tf + kMaxCluster * RG;           // [2][RG] cluster max and sum per row
+  float* xm = cl + RG;                         // merge: [kMergeSlots][16] running max
+  float* xl = xm + kMergeSlots * 16;           // merge: [kMergeSlots][16] sums
+  float* xo = xl + kMergeSlots * 16;           // merge: [kMergeSlots][16][4] outputs
 
   if (warp == kWarps) {
     // ------------------------------ producer -------------------------------------------
@@ -743,51 +733,139 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   }
   __syncthreads();
 
-  // ---- cluster merge through distributed shared memory -> one partial per cluster --------
+  // ---- this CTA's partial rows -> workspace; the row group's last CTAs merge them --------
   const size_t rows_all = (size_t)a.B * a.HQ * a.S;
-  float* gpart = P.gpart;  // [clusters][rows_all][D+4]
-  cluster_sync_all();
+  const int nsplit = gridDim.x;
   {
-    for (int k = threadIdx.x; k < csize * RG; k += kThreads) {
-      const int c = k / RG, r = k - c * RG;
-      tm[k] = ld_dsmem_f32(cm + r, c);
-      tl[k] = ld_dsmem_f32(cl + r, c);
-    }
-    __syncthreads();
-    if (threadIdx.x < RG) {
-      const int r = threadIdx.x;
-      float mx = kNegInf;
-      for (int c = 0; c < csize; ++c) mx = fmaxf(mx, tm[c * RG + r]);
-      const float mu = mx == kNegInf ? 0.f : mx;
-      float l = 0.f;
-      for (int c = 0; c < csize; ++c) {
-        const float f = ex2(tm[c * RG + r] - mu);
-        tf[c * RG + r] = f;
-        l += f * tl[c * RG + r];
-      }
-      ml[r] = mx;
-      ml[RG + r] = l;
-    }
-    __syncthreads();
-    const int n_el = rows_here * D;
-    for (int e = (int)crank * kThreads + threadIdx.x; e < n_el; e += csize * kThreads) {
+    float* gp = P.gpart + ((size_t)split * rows_all + row0 + rbase) * (D + 4);
+    for (int e = threadIdx.x; e < rows_here * D; e += kThreads) {
       const int r = e / D, d = e - r * D;
-      const int fe = frag_index<G, KS>(r, d);
-      float v = 0.f;
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c)
-        if (c < csize) v = fmaf(tf[c * RG + r], ld_dsmem_f32(cp + fe, c), v);
-      gpart[((size_t)cidx * rows_all + row0 + rbase + r) * (D + 4) + d] = v;
+      gp[(size_t)r * (D + 4) + d] = cp[frag_index<G, KS>(r, d)];
     }
-    if (crank == 0 && threadIdx.x < rows_here) {
-      const int r = threadIdx.x;
-      float* dst = gpart + ((size_t)cidx * rows_all + row0 + rbase + r) * (D + 4);
-      dst[D] = ml[r];
-      dst[D + 1] = ml[RG + r];
+    if (threadIdx.x < rows_here) {
+      gp[(size_t)threadIdx.x * (D + 4) + D] = cm[threadIdx.x];
+      gp[(size_t)threadIdx.x * (D + 4) + D + 1] = cl[threadIdx.x];
     }
   }
-  cluster_sync_all();  // every remote read of this CTA's shared memory is done
-
+  if (!P.merge) return;
+  // Arrival ticket (acq_rel at gpu scope: this CTA's rows, ordered before it by the barrier,
+  // are visible to whoever sees the count). The last `nm` arrivals merge one (row, 64-dim
+  // slice) unit each, after every CTA of the row group has arrived; all CTAs of the
+  // grid are co-resident (the planner sizes the split for one wave), so the wait ends.
+  __syncthreads();
+  __shared__ int s_ticket;
+  const int grp = blockIdx.z * gridDim.y + blockIdx.y;  // (b, kv head, row group)
+  int* arrive = P.counters + grp;
+  int* done = P.counters + kMaxCounters + grp;
+  if (threadIdx.x == 0) s_ticket = atom_add_acq_rel(arrive, 1);
+  __syncthreads();
+  constexpr int kSlices = D / 64;
+  const int units = kSlices * rows_here;
+  const int nm = min(nsplit, units);
+  const int ticket = s_ticket;
+  if (ticket < nsplit - nm) return;
+  if (threadIdx.x == 0) {
+    bool ok = ld_acquire(arrive) >= nsplit;
+    const unsigned long long t0 = ok ? 0ull : global_ns();
+    while (!ok) {
+      __nanosleep(64);
+      ok = ld_acquire(arrive) >= nsplit;
+      if (!ok && global_ns() - t0 > kSpinNanos) {
+        flag_device_error(a.status, 14);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const int q4 = threadIdx.x & 15, slot = threadIdx.x >> 4;  // 16 float4 columns x slots
+  static_assert(kThreads % 16 == 0 && D % 64 == 0, "merge layout");
+  for (int u = ticket - (nsplit - nm); u < units; u += nm) {
+    const int r = u / kSlices, sl = u - r * kSlices;
+    const size_t rowi = row0 + rbase + r;
+    float mt = kNegInf, lt = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    {
+      // this thread's partials: p = slot, slot + kMergeSlots, ... in batches of 8 (online)
+      for (int p0 = slot; p0 < nsplit; p0 += 8 * kMergeSlots) {
+        float pm[8], pl[8];
+        float4 po[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int p = p0 + k * kMergeSlots;
+          if (p < nsplit) {
+            const float* src = P.gpart + ((size_t)p * rows_all + rowi) * (D + 4);
+            pm[k] = __ldcg(src + D);
+            pl[k] = __ldcg(src + D + 1);
+            po[k] = __ldcg(reinterpret_cast<const float4*>(src + sl * 64) + q4);
+          } else {
+            pm[k] = kNegInf;
+            pl[k] = 0.f;
+            po[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        float mx = mt;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx = fmaxf(mx, pm[k]);
+        const float mu = mx == kNegInf ? 0.f : mx;
+        const float fr = ex2(mt - mu);
+        lt *= fr;
+        acc.x *= fr; acc.y *= fr; acc.z *= fr; acc.w *= fr;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float f = ex2(pm[k] - mu);
+          lt = fmaf(f, pl[k], lt);
+          acc.x = fmaf(f, po[k].x, acc.x);
+          acc.y = fmaf(f, po[k].y, acc.y);
+          acc.z = fmaf(f, po[k].z, acc.z);
+          acc.w = fmaf(f, po[k].w, acc.w);
+        }
+        mt = mx;
+      }
+      xm[slot * 16 + q4] = mt;
+      xl[slot * 16 + q4] = lt;
+      reinterpret_cast<float4*>(xo)[slot * 16 + q4] = acc;
+    }
+    __syncthreads();
+    if (slot == 0) {
+      float mx = kNegInf;
+#pragma unroll
+      for (int k = 0; k < kMergeSlots; ++k) mx = fmaxf(mx, xm[k * 16 + q4]);
+      const float mu = mx == kNegInf ? 0.f : mx;
+      float l = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < kMergeSlots; ++k) {
+        const float f = ex2(xm[k * 16 + q4] - mu);
+        const float4 v = reinterpret_cast<const float4*>(xo)[k * 16 + q4];
+        l = fmaf(f, xl[k * 16 + q4], l);
+        o.x = fmaf(f, v.x, o.x);
+        o.y = fmaf(f, v.y, o.y);
+        o.z = fmaf(f, v.z, o.z);
+        o.w = fmaf(f, v.w, o.w);
+      }
+      const int d0 = sl * 64 + 4 * q4;
+      if (a.out_kind == QKV_OUT_PARTIAL) {
+        float* dst = reinterpret_cast<float*>(a.out) + rowi * (D + 4);
+        *reinterpret_cast<float4*>(dst + d0) = o;
+        if (sl == 0 && q4 == 0) *reinterpret_cast<float4*>(dst + D) = make_float4(mx, l, 0.f, 0.f);
+      } else {
+        const float inv = l == 0.f ? 1.f : 1.f / l;
+        T* dst = reinterpret_cast<T*>(a.out) + rowi * D + d0;
+        dst[0] = Elem<T>::from_f32(o.x * inv);
+        dst[1] = Elem<T>::from_f32(o.y * inv);
+        dst[2] = Elem<T>::from_f32(o.z * inv);
+        dst[3] = Elem<T>::from_f32(o.w * inv);
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    // the last merger to finish returns the row group's counters to zero for the next call
+    if (atom_add_acq_rel(done, 1) == nm - 1) {
+      *arrive = 0;
+      *done = 0;
+    }
+  }
 }
 
 // One CTA (8 warps) per output row. Warp w owns partials w, w+8, ... (up to kCombineBatch
@@ -908,18 +986,18 @@ bool make_code_map(CUtensorMap* m, const void* base, int NP, long long bhs) {
   return make_code_map_bytes(m, base, GG::RB, NP, bhs, GG::RBOX, kBoxRows);
 }
 
-// Shared memory the epilogue needs (the stage ring is reused); the final merge also keeps
-// two floats per (row, cluster) there, bounded by the splits the planner allows.
+// Shared memory the epilogue needs (the stage ring is reused): per-warp rows, the CTA's
+// rows and the merge's per-slot running (max, sum, 4 outputs) of 16 float4 columns.
 template <int D, int NT>
 constexpr size_t merge_bytes() {
   constexpr int RG = 8 * NT;
   return ((size_t)kWarps * RG * 2 + (size_t)kWarps * RG * D + (size_t)RG * D + 2 * RG +
-          3 * kMaxCluster * RG + 2 * RG) *
+          (size_t)kMergeSlots * 16 * 6) *
          4;
 }
 
 template <typename T, int BITS, int D, int NT>
-int launch_split(const AttnArgs& a, cudaStream_t st) {
+int launch_split(const AttnArgs& a, bool merge, cudaStream_t st) {
   using CF = DecodeCfg<BITS, D, NT>;
   using GG = Geo<BITS, D, CF::TP, CF::RING>;
   constexpr int RG = 8 * NT;
@@ -929,8 +1007,10 @@ int launch_split(const AttnArgs& a, cudaStream_t st) {
   const size_t smem = std::max(ring, merge_bytes<D, NT>()) + 1024;  // + alignment slack
   DecodeParams p;
   p.a = a;
-  p.clusters = a.splits / a.cluster;
-  p.gpart = (float*)a.workspace;
+  p.merge = merge ? 1 : 0;
+  p.counters = reinterpret_cast<int*>(a.workspace);
+  p.gpart = reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
+                                     (merge ? kCounterBytes : 0));
   if (!make_code_map<BITS, D>(&p.tmk, a.kw, a.NP, (long long)a.B * a.HKV) ||
       !make_code_map<BITS, D>(&p.tmv, a.vw, a.NP, (long long)a.B * a.HKV))
     return QKV_ECUDA;
@@ -949,40 +1029,36 @@ int launch_split(const AttnArgs& a, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? QKV_OK : QKV_ECUDA;
 }
 
 template <typename T, int BITS, int NT>
-int launch_split_d(const AttnArgs& a, cudaStream_t st) {
+int launch_split_d(const AttnArgs& a, bool merge, cudaStream_t st) {
   switch (a.D) {
-    case 64: return launch_split<T, BITS, 64, NT>(a, st);
-    case 128: return launch_split<T, BITS, 128, NT>(a, st);
+    case 64: return launch_split<T, BITS, 64, NT>(a, merge, st);
+    case 128: return launch_split<T, BITS, 128, NT>(a, merge, st);
     case 256:
-      if constexpr (NT == 1) return launch_split<T, BITS, 256, NT>(a, st);
+      if constexpr (NT == 1) return launch_split<T, BITS, 256, NT>(a, merge, st);
       return QKV_EUNSUPPORTED;
     default: return QKV_EUNSUPPORTED;
   }
 }
 
 template <typename T, int NT>
-int launch_split_b(const AttnArgs& a, cudaStream_t st) {
-  return a.bits == 4 ? launch_split_d<T, 4, NT>(a, st) : launch_split_d<T, 8, NT>(a, st);
+int launch_split_b(const AttnArgs& a, bool merge, cudaStream_t st) {
+  return a.bits == 4 ? launch_split_d<T, 4, NT>(a, merge, st) : launch_split_d<T, 8, NT>(a, merge, st);
 }
 
-int launch_split_any(const AttnArgs& a, cudaStream_t st) {
+int launch_split_any(const AttnArgs& a, bool merge, cudaStream_t st) {
   const bool nt1 = decode_rows_per_group((a.HQ / a.HKV) * a.S, a.D) == 8;
   if (a.dtype == QKV_BF16)
-    return nt1 ? launch_split_b<__nv_bfloat16, 1>(a, st) : launch_split_b<__nv_bfloat16, 2>(a, st);
-  return nt1 ? launch_split_b<__half, 1>(a, st) : launch_split_b<__half, 2>(a, st);
+    return nt1 ? launch_split_b<__nv_bfloat16, 1>(a, merge, st) : launch_split_b<__nv_bfloat16, 2>(a, merge, st);
+  return nt1 ? launch_split_b<__half, 1>(a, merge, st) : launch_split_b<__half, 2>(a, merge, st);
 }
 
 }  // namespace
@@ -992,53 +1068,40 @@ int decode_rows_per_group(int R, int D) { return (R <= 8 || D > 128) ? 8 : 16; }
 
 namespace {
 
-// Co-resident clusters of `cl` CTAs for one decode instantiation on the current device
-// (cached); 0 when the query is unavailable (e.g. no device).
+// Co-resident CTAs of one decode instantiation on the current device (cached); 0 when the
+// query is unavailable (e.g. no device).
 template <int BITS, int D, int NT>
-int max_clusters(int cl) {
+int max_ctas() {
   using CF = DecodeCfg<BITS, D, NT>;
   using GG = Geo<BITS, D, CF::TP, CF::RING>;
-  constexpr int RG = 8 * NT;
-  static int cache[64][4];
-  static bool init[64][4];
+  static int cache[64];
+  static bool init[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
     return 0;
   }
-  const int ci = cl == 8 ? 3 : cl == 4 ? 2 : cl == 2 ? 1 : 0;
-  if (init[dev][ci]) return cache[dev][ci];
+  if (init[dev]) return cache[dev];
   const size_t ring = (size_t)GG::STAGES * GG::STAGE_BYTES;
   const size_t smem = std::max(ring, merge_bytes<D, NT>()) + 1024;
   auto kern = decode_kernel<__nv_bfloat16, BITS, D, NT>;
-  int n = 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
-      cudaSuccess) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(cl * 64, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cl;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess) n = 0;
-  }
+  int per_sm = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+    per_sm = 0;
   cudaGetLastError();
-  cache[dev][ci] = n;
-  init[dev][ci] = true;
-  return n;
+  cache[dev] = per_sm * num_sms();
+  init[dev] = true;
+  return cache[dev];
 }
 
-int max_clusters_any(int bits, int D, int R, int cl) {
+int max_ctas_any(int bits, int D, int R) {
   const bool nt1 = decode_rows_per_group(R, D) == 8;
 #define QKV_MC(BB, DD) \
-  if (bits == BB && D == DD) return nt1 ? max_clusters<BB, DD, 1>(cl) : max_clusters<BB, DD, 2>(cl);
+  if (bits == BB && D == DD) return nt1 ? max_ctas<BB, DD, 1>() : max_ctas<BB, DD, 2>();
   QKV_MC(4, 64) QKV_MC(4, 128) QKV_MC(8, 64) QKV_MC(8, 128)
-  if (D == 256) return bits == 4 ? max_clusters<4, 256, 1>(cl) : max_clusters<8, 256, 1>(cl);
+  if (D == 256) return bits == 4 ? max_ctas<4, 256, 1>() : max_ctas<8, 256, 1>();
 #undef QKV_MC
   return 0;
 }
@@ -1050,74 +1113,41 @@ int round_chunk(int n_max, int sp) {
 
 }  // namespace
 
-// Split plan: as many co-resident CTAs as the GPU holds in one wave, grouped in the
-// largest cluster size that loses at most ~8 % of those slots to cluster packing.
+// Split plan: as many co-resident CTAs as the GPU holds in one wave (the in-kernel merge's
+// last arrivals wait for the rest of their row group), at least 16 keys per split.
 void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want,
                  int* splits, int* chunk, int* cluster) {
   const int R = (HQ / HKV) * S;
   const int rgs = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
   const int units = std::max(1, B * HKV * rgs);
   const int max_sp = std::max(1, (std::max(n_max, 1) + 15) / 16);
+  int sp;
   if (want > 0) {
-    const int sp = want;
-    int cl = 1;
-    while (cl * 2 <= std::min(sp, kMaxCluster) && sp % (cl * 2) == 0) cl *= 2;
-    *splits = std::min(sp, kMaxClustersPerGroup * cl);
-    *cluster = cl;
-    *chunk = round_chunk(n_max, *splits);
-    return;
+    sp = want;
+  } else {
+    int slots = max_ctas_any(bits, D, R);
+    if (slots <= 0) slots = decode_ctas_per_sm(R, D, bits) * num_sms();  // no device to ask
+    sp = std::max(1, slots / units);
   }
-  int best_ctas = 0, best_cl = 1, best_i = 0;
-  int ctas[4] = {0, 0, 0, 0};
-  const int cls[4] = {1, 2, 4, 8};
-  for (int i = 0; i < 4; ++i) {
-    int mc = max_clusters_any(bits, D, R, cls[i]);
-    if (mc <= 0) mc = (i == 0 ? 1 : 0) * (decode_ctas_per_sm(R, D, bits) * num_sms());  // no query
-    ctas[i] = mc * cls[i];
-    if (ctas[i] > best_ctas) best_ctas = ctas[i];
-  }
-  for (int i = 3; i >= 0; --i) {
-    if (ctas[i] > 0 && ctas[i] * 100 >= best_ctas * 92) {
-      best_cl = cls[i];
-      best_i = i;
-      break;
-    }
-  }
-  int slots = ctas[best_i];
-  if (ctas[3] == 0 && ctas[2] == 0 && ctas[1] == 0) {  // no device to ask: heuristic
-    best_cl = 4;
-    slots = ctas[0] / 16 * 15;
-  }
-  slots = std::max(slots, best_cl);
-  int sp = std::max(1, slots / units);
-  sp = std::min(sp, max_sp);
-  int cl = best_cl;
-  while (cl > 1 && cl > sp) cl /= 2;
-  sp = std::max(cl, sp / cl * cl);
-  sp = std::min(sp, kMaxClustersPerGroup * cl);
+  sp = std::min(std::min(sp, max_sp), kMaxSplits);
   *splits = sp;
-  *cluster = cl;
+  *cluster = 1;
   *chunk = round_chunk(n_max, sp);
 }
 
 size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster) {
-  return (size_t)(splits / cluster) * B * HQ * S * (D + 4) * sizeof(float);
+  (void)cluster;
+  return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
 }
 
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster) {
   (void)HKV;
-  return decode_partials_bytes(B, HQ, S, D, splits, cluster);
+  return kCounterBytes + decode_partials_bytes(B, HQ, S, D, splits, cluster);
 }
 
-int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, st); }
+int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, false, st); }
 
-int launch_decode(const AttnArgs& a, cudaStream_t st) {
-  const int rc = launch_split_any(a, st);
-  if (rc != QKV_OK) return rc;
-  const long long rows = (long long)a.B * a.HQ * a.S;
-  return launch_combine((const float*)a.workspace, a.splits / a.cluster, rows, rows, a.D, a.out,
-                        a.dtype, a.out_kind, st);
-}
+int launch_decode(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, true, st); }
 
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
                    int D, void* out, int out_dtype, int out_kind, cudaStream_t st) {

@@ -15,9 +15,10 @@
 // address. Make that first call on a device before any stream capture begins.
 //
 // Sharing: every call on a device uses the same array, which keeps the last call's contents.
-// Each call writes every partial row before reading it, so nothing in it has to start at
-// zero. Two calls whose kernels overlap on the GPU (for example on two streams at once) race
-// on the array: serialize them.
+// Each call writes every partial row before reading it. The array's first 128 KiB hold the
+// per-row-group arrival counters of the attention kernel's merge: they start at zero (static
+// storage is zero-initialized) and every call returns them to zero. Two calls whose kernels
+// overlap on the GPU (for example on two streams at once) race on the array: serialize them.
 #include <algorithm>
 
 #include "../../include/qkv.h"

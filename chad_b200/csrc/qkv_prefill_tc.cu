@@ -647,7 +647,10 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
   prm.TT = p.tokens_per_tile;
   prm.chunk = p.chunk;
   const bool direct = combine && p.splits == 1 && a.out_kind == QKV_OUT_NORMALIZED;
-  prm.parts = direct ? nullptr : reinterpret_cast<float*>(a.workspace);
+  // attention calls keep the workspace's leading arrival counters intact (see kCounterBytes)
+  prm.parts = direct ? nullptr
+                     : reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
+                                                (combine ? kCounterBytes : 0));
   const size_t smem = (size_t)SM::BYTES + 1024;
   auto kern = prefill_tc_kernel<T, BITS, MT>;
   static unsigned attr_done = 0;
@@ -721,7 +724,7 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
 
 size_t prefill_tc_workspace_bytes(int B, int HQ, int S, int D, const TcPlan& p, bool direct) {
   if (direct && p.splits == 1) return 0;
-  return (size_t)p.splits * B * HQ * S * (D + 4) * sizeof(float);
+  return kCounterBytes + (size_t)p.splits * B * HQ * S * (D + 4) * sizeof(float);
 }
 
 int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {

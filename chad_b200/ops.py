@@ -121,7 +121,9 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     key = (dev.type, dev.index)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        # zeroed once: the leading arrival counters must start at zero (every call leaves
+        # them zero again)
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
         _WS[key] = ws
     return ws
 

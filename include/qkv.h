@@ -88,7 +88,13 @@ int qkv_dequantize(const void* w, const void* scales, const void* biases, void* 
                    long long rows, int D, int bits, int group_size, int dtype,
                    int round_mode, void* stream);
 
-/* Bytes of scratch that qkv_attention needs for these sizes (n_max = largest key count). */
+/*
+ * Bytes of scratch that qkv_attention needs for these sizes (n_max = largest key count).
+ * The workspace's first QKV_COUNTER_BYTES bytes hold arrival counters of the in-kernel
+ * merge: zero them once before the first call (cudaMemset); every call leaves them zero.
+ * One workspace serves one stream at a time.
+ */
+#define QKV_COUNTER_BYTES 131072
 size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int bits,
                           int group_size);
 
@@ -110,7 +116,9 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
  *             mask + b*mask_sb + h*mask_sh + s*mask_sq + k, for k < mask_nk (mask_nk >= key
  *             count); a stride of 0 broadcasts
  *   splits:   split count along the keys (0 = choose from the SM count)
- *   workspace: >= qkv_workspace_size(B, HQ, HKV, S, D, max key count, bits, group_size)
+ *   workspace: >= qkv_workspace_size(B, HQ, HKV, S, D, max key count, bits, group_size),
+ *             its first QKV_COUNTER_BYTES zeroed before the first call (left zero by every
+ *             call)
  */
 int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
                   const void* vw, const void* vs, const void* vb, void* out,
