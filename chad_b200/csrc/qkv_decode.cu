@@ -155,14 +155,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
-  int old;
-  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -182,7 +185,7 @@ struct DecodeParams {
   CUtensorMap tmk;  // K codes: (RB bytes, NP, B*HKV)
   CUtensorMap tmv;  // V codes
   float* gpart;     // per-CTA partial rows [splits][B*HQ*S][D+4]
-  int* counters;    // [2][kMaxCounters] arrivals and finished mergers per row group
+  unsigned* counters;  // [kMaxCounters] arrival generations per row group
   int merge;        // 1: the row group's last CTAs merge the partials into a.out
 };
 
@@ -199,7 +202,6 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   // swizzled TMA tiles need 1024-byte aligned stage buffers: align by hand
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full_bar[4], empty_bar[4];
-  __shared__ __align__(16) T q_sh[RG * D];  // this CTA's query rows
 
   const AttnArgs& a = P.a;
   // Programmatic dependent launch: the next kernel in the stream may be scheduled as soon as
@@ -310,31 +312,34 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     // -------------------------------- consumers -----------------------------------------
     const T* qg = (const T*)a.q;
     const float qmul = a.scale * 1.4426950408889634f;  // softmax in base 2
-    {
-      // the CTA's RG query rows (contiguous in q) into shared memory, 16 bytes per lane
-      constexpr int V16 = RG * D * (int)sizeof(T) / 16;
-      const uint4* src = reinterpret_cast<const uint4*>(qg + (row0 + rbase) * D);
-      uint4* dst = reinterpret_cast<uint4*>(q_sh);
-      const int valid16 = rows_here * D * (int)sizeof(T) / 16;
-      for (int k = threadIdx.x; k < V16; k += kWarps * 32)
-        dst[k] = k < valid16 ? src[k] : make_uint4(0u, 0u, 0u, 0u);
-      named_bar_sync(1, kWarps * 32);
-    }
-
     // Q as the B operand of QK, per scale group: k = head_dim pairs in this lane's code
-    // order (the 4-bit "x16" slots pre-divided by 16), n = query row. The group sums of the
-    // same f16 values feed the bias term.
+    // order (the 4-bit "x16" slots pre-divided by 16), n = query row. A lane's fragments of
+    // one group are the 16 consecutive head dims 64g + 16tq .. +15 of row gq: two 16-byte
+    // loads straight from global memory, all issued before any is used. The group sums of
+    // the same f16 values feed the bias term.
     uint32_t qf[NT][G][KS][2];
     float qsum_mine[NT][G];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int r = rbase + nt * 8 + gq;
       const bool rv = r < R;
-      const T* qr = q_sh + (nt * 8 + gq) * D;
+      const T* qr = qg + (row0 + (rv ? r : 0)) * D;
+      uint4 raw[G][2];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
+        const uint4* src = reinterpret_cast<const uint4*>(qr + 64 * g + 16 * tq);
+        raw[g][0] = rv ? src[0] : make_uint4(0u, 0u, 0u, 0u);
+        raw[g][1] = rv ? src[1] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint32_t w[8] = {raw[g][0].x, raw[g][0].y, raw[g][0].z, raw[g][0].w,
+                               raw[g][1].x, raw[g][1].y, raw[g][1].z, raw[g][1].w};
+        auto qv = [&](int d) {  // dim d of the 16-dim slice, scaled, rounded to f16
+          const uint32_t bitsv = (d & 1) ? (w[d >> 1] >> 16) : (w[d >> 1] & 0xffffu);
+          return __half2float(__float2half_rn(Elem<T>::bits_to_f32((uint16_t)bitsv) * qmul));
+        };
         float acc = 0.f;
-        const int base = 64 * g + 16 * tq;
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
           int d0, d1, d2, d3;
@@ -350,10 +355,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
             d2 = d0 + 1;
             d3 = d0 + 3;
           }
-          const float v0 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d0]) * qmul)) : 0.f;
-          const float v1 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d1]) * qmul)) : 0.f;
-          const float v2 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d2]) * qmul)) : 0.f;
-          const float v3 = rv ? __half2float(__float2half_rn(Elem<T>::to_f32(qr[base + d3]) * qmul)) : 0.f;
+          const float v0 = qv(d0), v1 = qv(d1), v2 = qv(d2), v3 = qv(d3);
           acc += (v0 + v1) + (v2 + v3);
           const float hs = BITS == 4 ? 0.0625f : 1.f;
           qf[nt][g][k][0] = pack_f16x2(v0, v1);
@@ -749,27 +751,33 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   }
   if (!P.merge) return;
   // Arrival ticket (acq_rel at gpu scope: this CTA's rows, ordered before it by the barrier,
-  // are visible to whoever sees the count). The last `nm` arrivals merge one (row, 64-dim
-  // slice) unit each, after every CTA of the row group has arrived; all CTAs of the
-  // grid are co-resident (the planner sizes the split for one wave), so the wait ends.
+  // are visible to whoever sees the count). The row group's counter advances by exactly
+  // 1024 per call: one per CTA, and the last arrival adds the rest, so the low 10 bits
+  // are this call's ticket and nothing needs resetting. The last `nm` arrivals merge one
+  // (row, 64-dim slice) unit each once the generation is complete; every CTA of the row
+  // group is resident before any of them waits (one wave, dispatched in order).
   __syncthreads();
-  __shared__ int s_ticket;
+  __shared__ unsigned s_ticket;
   const int grp = blockIdx.z * gridDim.y + blockIdx.y;  // (b, kv head, row group)
-  int* arrive = P.counters + grp;
-  int* done = P.counters + kMaxCounters + grp;
-  if (threadIdx.x == 0) s_ticket = atom_add_acq_rel(arrive, 1);
+  unsigned* arrive = P.counters + grp;
+  if (threadIdx.x == 0) {
+    const unsigned old = atom_add_acq_rel(arrive, 1u);
+    if ((old & 1023u) == (unsigned)nsplit - 1u) red_add_release(arrive, 1024u - (unsigned)nsplit);
+    s_ticket = old;
+  }
   __syncthreads();
   constexpr int kSlices = D / 64;
   const int units = kSlices * rows_here;
   const int nm = min(nsplit, units);
-  const int ticket = s_ticket;
+  const unsigned base = s_ticket & ~1023u;
+  const int ticket = (int)(s_ticket & 1023u);
   if (ticket < nsplit - nm) return;
   if (threadIdx.x == 0) {
-    bool ok = ld_acquire(arrive) >= nsplit;
+    bool ok = ld_acquire(arrive) - base >= 1024u;
     const unsigned long long t0 = ok ? 0ull : global_ns();
     while (!ok) {
       __nanosleep(64);
-      ok = ld_acquire(arrive) >= nsplit;
+      ok = ld_acquire(arrive) - base >= 1024u;
       if (!ok && global_ns() - t0 > kSpinNanos) {
         flag_device_error(a.status, 14);
         break;
@@ -859,13 +867,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) {
-    // the last merger to finish returns the row group's counters to zero for the next call
-    if (atom_add_acq_rel(done, 1) == nm - 1) {
-      *arrive = 0;
-      *done = 0;
-    }
-  }
+
 }
 
 // One CTA (8 warps) per output row. Warp w owns partials w, w+8, ... (up to kCombineBatch
@@ -1008,7 +1010,7 @@ int launch_split(const AttnArgs& a, bool merge, cudaStream_t st) {
   DecodeParams p;
   p.a = a;
   p.merge = merge ? 1 : 0;
-  p.counters = reinterpret_cast<int*>(a.workspace);
+  p.counters = reinterpret_cast<unsigned*>(a.workspace);
   p.gpart = reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
                                      (merge ? kCounterBytes : 0));
   if (!make_code_map<BITS, D>(&p.tmk, a.kw, a.NP, (long long)a.B * a.HKV) ||

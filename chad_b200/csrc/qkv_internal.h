@@ -55,9 +55,10 @@ struct AttnArgs {
 // Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
 // Upper bound on (batch x kv heads x query-row groups) per call.
 constexpr int kMaxCounters = 16384;
-// Attention calls keep [2][kMaxCounters] int arrival counters at the start of the workspace
-// (zero before the first call, zero again after every call); partial rows follow them.
-constexpr size_t kCounterBytes = 2 * kMaxCounters * sizeof(int);
+// Attention calls keep kMaxCounters arrival counters (and room for as many more) at the
+// start of the workspace: zero before the first call; each call advances a row group's
+// counter by a whole 1024 (it is never reset). Partial rows follow.
+constexpr size_t kCounterBytes = 2 * kMaxCounters * sizeof(unsigned);
 int decode_rows_per_group(int R, int D);    // query rows handled by one CTA (8 or 16)
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster);
 size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster);
