@@ -6,7 +6,9 @@ the CUDA library and enqueues on torch's current stream.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import functools
 import math
 from typing import Optional, Sequence, Tuple, Union
 
@@ -50,6 +52,14 @@ def _need_cuda(*ts: torch.Tensor) -> torch.device:
     return dev
 
 
+def _on(dev: torch.device):
+    """Context making `dev` current; a no-op when it already is (the common case: switching
+    devices on every call costs more than the rest of the host-side work)."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
+
+
 def _contig(t: torch.Tensor, name: str) -> torch.Tensor:
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
@@ -69,7 +79,7 @@ def quantize_append(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     b, h, s, d = x.shape
     np_ = w.shape[2]
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(lib.qkv_quantize_append(x.data_ptr(), dtype_code(x), w.data_ptr(),
                                       scales.data_ptr(), biases.data_ptr(), b, h, s, d, np_,
                                       offset, bits, group_size, dtype_code(scales),
@@ -98,7 +108,7 @@ def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits
     rows = w.numel() // w.shape[-1]
     out = torch.empty((*w.shape[:-1], d), dtype=scales.dtype, device=w.device)
     lib = _lib.load()
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(lib.qkv_dequantize(_contig(w, "w").data_ptr(), _contig(scales, "scales").data_ptr(),
                                  _contig(biases, "biases").data_ptr(), out.data_ptr(), rows, d,
                                  bits, group_size, dtype_code(scales), round_mode, _stream(dev)))
@@ -114,6 +124,14 @@ _WS = {}
 
 def workspace_size(B: int, HQ: int, HKV: int, S: int, D: int, n_max: int, bits: int,
                    group_size: int = GROUP_SIZE) -> int:
+    return _workspace_size(torch.cuda.current_device() if torch.cuda.is_available() else -1,
+                           B, HQ, HKV, S, D, n_max, bits, group_size)
+
+
+@functools.lru_cache(maxsize=4096)
+def _workspace_size(device: int, B: int, HQ: int, HKV: int, S: int, D: int, n_max: int,
+                    bits: int, group_size: int) -> int:
+    # the split plan depends on the current device's SM count: memoized per device
     return int(_lib.load().qkv_workspace_size(B, HQ, HKV, S, D, n_max, bits, group_size))
 
 
@@ -191,7 +209,7 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
     if splits:
         need = max(need, splits * B * HQ * S * (D + 4) * 4 + (1 << 16))
     ws = workspace if workspace is not None else _workspace(dev, need)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(lib.qkv_attention(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
                                 vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(),
                                 B, HQ, HKV, S, D, NP, n, _ptr(lens), _ptr(pos_base),
@@ -219,7 +237,7 @@ def partials(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequence
         parts = torch.empty(need // 4, dtype=torch.float32, device=q.device)
     kind, m, mnk, sb, sh, sq = _mask_args(mask, q, n)
     np_out = ctypes.c_int(0)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(_lib.load().qkv_partials(
             q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(), vw.data_ptr(),
             vs.data_ptr(), vb.data_ptr(), parts.data_ptr(), parts.numel() * parts.element_size(),
@@ -242,7 +260,7 @@ def combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
         out = torch.empty((*parts.shape[1:-1], d), dtype=out_dtype, device=parts.device)
     else:
         out = torch.empty(parts.shape[1:], dtype=torch.float32, device=parts.device)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(_lib.load().qkv_combine(parts.data_ptr(), p, rows, d, out.data_ptr(),
                                       dtype_code(out_dtype), out_kind, _stream(dev)))
     return out
@@ -260,7 +278,7 @@ def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     out = torch.empty_like(q)
     need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size)
     ws = _workspace(dev, need)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(_lib.load().qkv_prefill(
             _contig(q, "q").data_ptr(), _contig(k_new, "k_new").data_ptr(),
             _contig(v_new, "v_new").data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
