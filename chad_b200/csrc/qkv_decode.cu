@@ -45,7 +45,8 @@ namespace {
 constexpr int kWarps = 4;                    // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kBoxRows = 64;                 // key rows per TMA box
-constexpr int kMergeSlots = kThreads / 16;  // partial subsets merged side by side per unit
+constexpr int kMergeCols = 8;                     // float4 columns of one merge unit (32 dims)
+constexpr int kMergeSlots = kThreads / kMergeCols;  // partial subsets merged side by side
 constexpr int kMaxSplits = 256;              // bounds the merge's loads per thread
 #define kNegInf (-__int_as_float(0x7f800000))
 
@@ -288,9 +289,9 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   float* cp = ow + kWarps * RG * D;            // [RG*D] this CTA's output, fragment order
   float* cm = cp + RG * D;                     // [RG] this CTA's max per row
   float* cl = cm + RG;                         // [RG] this CTA's sum per row
-  float* xm = cl + RG;                         // merge: [kMergeSlots][16] running max
-  float* xl = xm + kMergeSlots * 16;           // merge: [kMergeSlots][16] sums
-  float* xo = xl + kMergeSlots * 16;           // merge: [kMergeSlots][16][4] outputs
+  float* xm = cl + RG;                         // merge: [kMergeSlots][kMergeCols] running max
+  float* xl = xm + kMergeSlots * kMergeCols;   // merge: [kMergeSlots][kMergeCols] sums
+  float* xo = xl + kMergeSlots * kMergeCols;   // merge: [kMergeSlots][kMergeCols][4] outputs
 
   if (warp == kWarps) {
     // ------------------------------ producer -------------------------------------------
@@ -754,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   // are visible to whoever sees the count). The row group's counter advances by exactly
   // 1024 per call: one per CTA, and the last arrival adds the rest, so the low 10 bits
   // are this call's ticket and nothing needs resetting. The last `nm` arrivals merge one
-  // (row, 64-dim slice) unit each once the generation is complete; every CTA of the row
+  // (row, 32-dim slice) unit each once the generation is complete; every CTA of the row
   // group is resident before any of them waits (one wave, dispatched in order).
   __syncthreads();
   __shared__ unsigned s_ticket;
@@ -766,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     s_ticket = old;
   }
   __syncthreads();
-  constexpr int kSlices = D / 64;
+  constexpr int kSlices = D / (4 * kMergeCols);
   const int units = kSlices * rows_here;
   const int nm = min(nsplit, units);
   const unsigned base = s_ticket & ~1023u;
@@ -785,8 +786,8 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     }
   }
   __syncthreads();
-  const int q4 = threadIdx.x & 15, slot = threadIdx.x >> 4;  // 16 float4 columns x slots
-  static_assert(kThreads % 16 == 0 && D % 64 == 0, "merge layout");
+  const int q4 = threadIdx.x % kMergeCols, slot = threadIdx.x / kMergeCols;  // columns x slots
+  static_assert(kThreads % kMergeCols == 0 && D % (4 * kMergeCols) == 0, "merge layout");
   for (int u = ticket - (nsplit - nm); u < units; u += nm) {
     const int r = u / kSlices, sl = u - r * kSlices;
     const size_t rowi = row0 + rbase + r;
@@ -804,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
             const float* src = P.gpart + ((size_t)p * rows_all + rowi) * (D + 4);
             pm[k] = __ldcg(src + D);
             pl[k] = __ldcg(src + D + 1);
-            po[k] = __ldcg(reinterpret_cast<const float4*>(src + sl * 64) + q4);
+            po[k] = __ldcg(reinterpret_cast<const float4*>(src + sl * 4 * kMergeCols) + q4);
           } else {
             pm[k] = kNegInf;
             pl[k] = 0.f;
@@ -829,29 +830,29 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         }
         mt = mx;
       }
-      xm[slot * 16 + q4] = mt;
-      xl[slot * 16 + q4] = lt;
-      reinterpret_cast<float4*>(xo)[slot * 16 + q4] = acc;
+      xm[slot * kMergeCols + q4] = mt;
+      xl[slot * kMergeCols + q4] = lt;
+      reinterpret_cast<float4*>(xo)[slot * kMergeCols + q4] = acc;
     }
     __syncthreads();
     if (slot == 0) {
       float mx = kNegInf;
 #pragma unroll
-      for (int k = 0; k < kMergeSlots; ++k) mx = fmaxf(mx, xm[k * 16 + q4]);
+      for (int k = 0; k < kMergeSlots; ++k) mx = fmaxf(mx, xm[k * kMergeCols + q4]);
       const float mu = mx == kNegInf ? 0.f : mx;
       float l = 0.f;
       float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int k = 0; k < kMergeSlots; ++k) {
-        const float f = ex2(xm[k * 16 + q4] - mu);
-        const float4 v = reinterpret_cast<const float4*>(xo)[k * 16 + q4];
-        l = fmaf(f, xl[k * 16 + q4], l);
+        const float f = ex2(xm[k * kMergeCols + q4] - mu);
+        const float4 v = reinterpret_cast<const float4*>(xo)[k * kMergeCols + q4];
+        l = fmaf(f, xl[k * kMergeCols + q4], l);
         o.x = fmaf(f, v.x, o.x);
         o.y = fmaf(f, v.y, o.y);
         o.z = fmaf(f, v.z, o.z);
         o.w = fmaf(f, v.w, o.w);
       }
-      const int d0 = sl * 64 + 4 * q4;
+      const int d0 = sl * 4 * kMergeCols + 4 * q4;
       if (a.out_kind == QKV_OUT_PARTIAL) {
         float* dst = reinterpret_cast<float*>(a.out) + rowi * (D + 4);
         *reinterpret_cast<float4*>(dst + d0) = o;
@@ -994,7 +995,7 @@ template <int D, int NT>
 constexpr size_t merge_bytes() {
   constexpr int RG = 8 * NT;
   return ((size_t)kWarps * RG * 2 + (size_t)kWarps * RG * D + (size_t)RG * D + 2 * RG +
-          (size_t)kMergeSlots * 16 * 6) *
+          (size_t)kMergeSlots * kMergeCols * 6) *
          4;
 }
 
