@@ -45,6 +45,7 @@ namespace {
 constexpr int kWarps = 4;                    // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kBoxRows = 64;                 // key rows per TMA box
+constexpr float kLazyLog2 = 4.0f;  // softmax max is only raised when exceeded by 2^4
 constexpr int kMergeCols = 8;                     // float4 columns of one merge unit (32 dims)
 constexpr int kMergeSlots = kThreads / kMergeCols;  // partial subsets merged side by side
 constexpr int kMaxSplits = 256;              // bounds the merge's loads per thread
@@ -545,20 +546,37 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         uint32_t pf[kSub][NT][G][2];
         bool rescale = false;
         float fac[NT][2];
+        // Lazy running max: the cross-lane reduction (and the rescale) only runs when some
+        // lane's score exceeds the running max by more than 2^kLazyLog2; otherwise the stale
+        // max stands and p stays <= 2^kLazyLog2 (P*scale remains well inside f16).
+        float mloc[NT][2];
+        bool need = false;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          float p[kSub][4];
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             float mt = fmaxf(s[0][nt][c], s[0][nt][2 + c]);
 #pragma unroll
             for (int h = 1; h < kSub; ++h) mt = fmaxf(mt, fmaxf(s[h][nt][c], s[h][nt][2 + c]));
-            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-            const float m_new = fmaxf(m_run[nt][c], mt);
+            mloc[nt][c] = mt;
+            need |= mt > m_run[nt][c] + kLazyLog2;
+          }
+        const bool full = __any_sync(0xffffffffu, need);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float p[kSub][4];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float m_new = m_run[nt][c];
+            if (full) {
+              float mt = mloc[nt][c];
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+              m_new = fmaxf(m_new, mt);
+            }
             const float m_use = m_new == kNegInf ? 0.f : m_new;
-            fac[nt][c] = ex2(m_run[nt][c] - m_use);
+            fac[nt][c] = full ? ex2(m_run[nt][c] - m_use) : 1.f;
             rescale |= m_new != m_run[nt][c];
             float lsum = 0.f;
             float ob[G];
