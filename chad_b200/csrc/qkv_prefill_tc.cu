@@ -275,16 +275,56 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     tc::tmem_alloc(&tmem_sh, 512);
     tc::tmem_relinquish();
   }
-  // ---- stage Q (all threads): MT tiles x 128 rows x 16 chunks of 8 head dims -------------
+  // ---- dequantizer state; the first tile's codes are requested before Q is staged --------
+  const bool is_dq = warp == 1 || warp == 2 || warp == 3 || warp == 12;
+  const int dq_row = (warp == 12 ? 3 : warp - 1) * 32 + lane;  // key row of each tile, 0..127
+  const uint8_t* kw_base = reinterpret_cast<const uint8_t*>(a.kw) + (long long)bh * a.NP * RB;
+  const uint8_t* vw_base = reinterpret_cast<const uint8_t*>(a.vw) + (long long)bh * a.NP * RB;
+  const long long sc0 = (long long)bh * a.NP * 4;  // 2 groups x 16 bit per key
+  uint32_t kc[RW], vc[RW], ksc = 0, kbi = 0, vsc = 0, vbi = 0;
+  auto load = [&](int i) {  // codes and scales of key row dq_row of tile i
+    const int key = k_begin + i * kKT + dq_row;
+    if (key < n) {
+#pragma unroll
+      for (int u = 0; u < RW / 4; ++u) {
+        const uint4 kv = ldg16(kw_base + (long long)key * RB + u * 16);
+        const uint4 vv = ldg16(vw_base + (long long)key * RB + u * 16);
+        kc[4 * u] = kv.x; kc[4 * u + 1] = kv.y; kc[4 * u + 2] = kv.z; kc[4 * u + 3] = kv.w;
+        vc[4 * u] = vv.x; vc[4 * u + 1] = vv.y; vc[4 * u + 2] = vv.z; vc[4 * u + 3] = vv.w;
+      }
+      ksc = ldg4((const uint8_t*)a.ks + sc0 + (long long)key * 4);
+      kbi = ldg4((const uint8_t*)a.kb + sc0 + (long long)key * 4);
+      vsc = ldg4((const uint8_t*)a.vs + sc0 + (long long)key * 4);
+      vbi = ldg4((const uint8_t*)a.vb + sc0 + (long long)key * 4);
+    }
+  };
+  if (is_dq && ntiles > 0) load(0);
+  // ---- stage Q (all threads): MT tiles x 128 rows x 16 chunks of 8 head dims; every load of
+  // a thread is issued before its first store -----------------------------------------------
   {
     const T* q = reinterpret_cast<const T*>(a.q);
-    for (int i = threadIdx.x; i < MT * 128 * 16; i += kThreadsTc) {
-      const int m = i / (128 * 16), r = (i / 16) % 128, c = i % 16;
-      const int hl = r / TT, t = t0 + m * TT + (r % TT);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (hl < gqa && t < a.S) {
-        const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
-        v = *reinterpret_cast<const uint4*>(q + row * kD + c * 8);
+    constexpr int kChunks = MT * 128 * 16;
+    constexpr int kPer = (kChunks + kThreadsTc - 1) / kThreadsTc;
+    uint4 qv[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + k * kThreadsTc;
+      qv[k] = make_uint4(0, 0, 0, 0);
+      if (i < kChunks) {
+        const int m = i / (128 * 16), r = (i / 16) % 128, c = i % 16;
+        const int hl = r / TT, t = t0 + m * TT + (r % TT);
+        if (hl < gqa && t < a.S) {
+          const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
+          qv[k] = *reinterpret_cast<const uint4*>(q + row * kD + c * 8);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + k * kThreadsTc;
+      if (i < kChunks) {
+        const int m = i / (128 * 16), r = (i / 16) % 128, c = i % 16;
+        uint4 v = qv[k];
         if constexpr (BITS == 4) {  // (0,1)(2,3)(4,5)(6,7) -> (0,4)(1,5)(2,6)(3,7)
           const uint4 u = v;
           v.x = prmt(u.x, u.z, 0x5410);
@@ -292,9 +332,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           v.z = prmt(u.y, u.w, 0x5410);
           v.w = prmt(u.y, u.w, 0x7632);
         }
+        const int h = c >> 3, cc = (c & 7) ^ (r & 7);
+        *reinterpret_cast<uint4*>(smem + SM::Q + m * 32768 + h * 16384 + r * 128 + cc * 16) = v;
       }
-      const int h = c >> 3, cc = (c & 7) ^ (r & 7);
-      *reinterpret_cast<uint4*>(smem + SM::Q + m * 32768 + h * 16384 + r * 128 + cc * 16) = v;
     }
   }
   fence_proxy_async_smem();
@@ -573,29 +613,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         *reinterpret_cast<float4*>(dst) = make_float4(m_run, l_run, 0.f, 0.f);
       }
     }
-  } else if (warp == 1 || warp == 2 || warp == 3 || warp == 12) {
+  } else if (is_dq) {
     // ---------------------------------------------------------------- dequantizers
-    const int row = (warp == 12 ? 3 : warp - 1) * 32 + lane;  // key row of each tile, 0..127
-    const uint8_t* kw_base = reinterpret_cast<const uint8_t*>(a.kw) + (long long)bh * a.NP * RB;
-    const uint8_t* vw_base = reinterpret_cast<const uint8_t*>(a.vw) + (long long)bh * a.NP * RB;
-    const long long sc0 = (long long)bh * a.NP * 4;  // 2 groups x 16 bit per key
-    uint32_t kc[RW], vc[RW], ksc = 0, kbi = 0, vsc = 0, vbi = 0;
-    auto load = [&](int i) {  // codes and scales of key row `row` of tile i
-      const int key = k_begin + i * kKT + row;
-      if (key < n) {
-#pragma unroll
-        for (int u = 0; u < RW / 4; ++u) {
-          const uint4 kv = ldg16(kw_base + (long long)key * RB + u * 16);
-          const uint4 vv = ldg16(vw_base + (long long)key * RB + u * 16);
-          kc[4 * u] = kv.x; kc[4 * u + 1] = kv.y; kc[4 * u + 2] = kv.z; kc[4 * u + 3] = kv.w;
-          vc[4 * u] = vv.x; vc[4 * u + 1] = vv.y; vc[4 * u + 2] = vv.z; vc[4 * u + 3] = vv.w;
-        }
-        ksc = ldg4((const uint8_t*)a.ks + sc0 + (long long)key * 4);
-        kbi = ldg4((const uint8_t*)a.kb + sc0 + (long long)key * 4);
-        vsc = ldg4((const uint8_t*)a.vs + sc0 + (long long)key * 4);
-        vbi = ldg4((const uint8_t*)a.vb + sc0 + (long long)key * 4);
-      }
-    };
+    const int row = dq_row;
     auto store = [&](const uint32_t* codes, uint32_t sc, uint32_t bi, bool valid, uint8_t* dst) {
       if (valid) {
         dequant_row<T, BITS>(codes, prmt(sc, 0u, 0x1010), prmt(sc, 0u, 0x3232),
@@ -607,7 +627,6 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
               make_uint4(0, 0, 0, 0);
       }
     };
-    if (ntiles > 0) load(0);
     for (int i = 0; i < ntiles; ++i) {
       const int buf = i & 1;
       const bool valid = k_begin + i * kKT + row < n;
