@@ -294,7 +294,7 @@ int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, 
                       mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes, false);
   if (rc) return rc;
   a.out_kind = QKV_OUT_PARTIAL;
-  *n_parts = a.use_tc ? a.tc.splits : a.splits / a.cluster;
+  *n_parts = a.use_tc ? a.tc.parts : a.splits / a.cluster;
   rc = a.use_tc ? launch_prefill_tc(a, a.tc, false, static_cast<cudaStream_t>(stream))
                 : launch_split_only(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "partials: unsupported configuration");

@@ -15,6 +15,7 @@ struct TcPlan {
   int tblocks;          // CTAs along the query tokens
   int splits;           // CTAs along the keys
   int chunk;            // keys per split (multiple of the 128-key tile)
+  int parts;            // partial rows per output row (splits, x2 when tiles == 1)
 };
 
 // Everything one attention launch needs (device pointers; sizes already validated).

@@ -225,8 +225,14 @@ __device__ __forceinline__ uint32_t ldg4(const void* p) {
   return v;
 }
 
-template <typename T, int BITS, int MT>
+// SK ("key-split tiles", MT == 2): the CTA's query rows fit one 128-row tile; both
+// tensor-memory tiles hold those rows and take alternate key tiles (tile m: keys tiles
+// m, m+2, ...), so one tile's softmax still overlaps the other's MMAs. Each tile writes its
+// own partial rows (partial 2*split + m).
+template <typename T, int BITS, int MT, bool SK>
 __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_constant__ TcParams P) {
+  static_assert(!SK || MT == 2, "key-split tiles need both tensor-memory tiles");
+  constexpr int QT = SK ? 1 : MT;  // query tiles staged
   using SM = TcSmem<MT>;
   using PK = Pack16<T>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -245,13 +251,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   const int gqa = a.HQ / a.HKV;
   const int bh = blockIdx.y;  // b * HKV + hkv
   const int b = bh / a.HKV, hkv = bh % a.HKV;
-  const int t0 = blockIdx.x * (MT * TT);
+  const int t0 = blockIdx.x * (QT * TT);
   const int split = blockIdx.z;
   const int n = min(max(a.n, 0), a.NP);
   const bool causal = a.mask_kind == QKV_MASK_CAUSAL;
   // key range of this CTA: [k_begin, k_stop); every row sees at most keys < k_stop
   const int k_begin = split * P.chunk;
-  const int t_last = min(t0 + MT * TT, a.S) - 1;
+  const int t_last = min(t0 + QT * TT, a.S) - 1;
   const int lim_hi = causal ? n - a.S + t_last : n - 1;  // last key any row may see
   const int k_stop = min(min(k_begin + P.chunk, n), lim_hi + 1);
   const int ntiles = k_stop > k_begin ? (k_stop - k_begin + kKT - 1) / kKT : 0;
@@ -303,7 +309,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   // a thread is issued before its first store -----------------------------------------------
   {
     const T* q = reinterpret_cast<const T*>(a.q);
-    constexpr int kChunks = MT * 128 * 16;
+    constexpr int kChunks = QT * 128 * 16;
     constexpr int kPer = (kChunks + kThreadsTc - 1) / kThreadsTc;
     uint4 qv[kPer];
 #pragma unroll
@@ -354,10 +360,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       const uint32_t vd_base = smem_u32(smem + SM::VD);
       auto qk = [&](int m, int i) {  // S_m = Q_m K(i)^T
         const uint32_t kb = kd_base + (i & 1) * kTileBytes;
+        const uint32_t qb = q_base + (SK ? 0 : m) * 32768;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint64_t ad =
-              tc::sdesc_sw128(q_base + m * 32768 + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
+          const uint64_t ad = tc::sdesc_sw128(qb + (s >> 2) * 16384 + (s & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sdesc_sw128(kb + (s >> 2) * kHalf + (s & 3) * 32, 16, 1024);
           tc::mma_ss(tmem + m * 128, ad, bd, id_s, s > 0 ? 1u : 0u);
         }
@@ -369,10 +375,41 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         for (int s = 0; s < kKT / 16; ++s) {
           const uint64_t bd = tc::sdesc_sw128(vb + s * 2048, kHalf, 1024);
           tc::mma_ts(tmem + 256 + m * 128, tmem + m * 128 + s * 8, bd, id_o,
-                     (i > 0 || s > 0) ? 1u : 0u);
+                     (i > (SK ? m : 0) || s > 0) ? 1u : 0u);
         }
         tc::mma_commit(&o_done[m]);
       };
+      if constexpr (SK) {
+        // tile m takes key tiles m, m+2, ...: each QK / PV touches one tile's buffers
+        for (int m = 0; m < 2 && ok; ++m) {
+          if (m < ntiles) {
+            ok = mbar_wait(&k_full[m], 0, a.status, 40);
+            if (!ok) break;
+            tc::fence_after_sync();
+            qk(m, m);
+            tc::mma_commit(&k_free[m]);
+          }
+        }
+        for (int j = 0; 2 * j < ntiles && ok; ++j) {
+          for (int m = 0; m < 2 && ok; ++m) {
+            const int i = 2 * j + m;
+            if (i >= ntiles) break;
+            ok = mbar_wait(&v_full[i & 1], (i >> 1) & 1, a.status, 41);
+            if (ok) ok = mbar_wait(&p_full[m], j & 1, a.status, 42);
+            if (!ok) break;
+            tc::fence_after_sync();
+            pv(m, i);
+            tc::mma_commit(&v_free[i & 1]);
+            if (i + 2 < ntiles) {
+              ok = mbar_wait(&k_full[i & 1], ((i + 2) >> 1) & 1, a.status, 43);
+              if (!ok) break;
+              tc::fence_after_sync();
+              qk(m, i + 2);  // S_m is free: P_m(i) is read by the PV issued just before
+              tc::mma_commit(&k_free[i & 1]);
+            }
+          }
+        }
+      } else {
       if (ntiles > 0) {
         ok = mbar_wait(&k_full[0], 0, a.status, 40);
         if (ok) {
@@ -402,6 +439,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         tc::mma_commit(&v_free[i & 1]);
         if (more) tc::mma_commit(&k_free[(i + 1) & 1]);
       }
+      }
       tc::mma_commit(&mma_fin);
       mbar_wait(&mma_fin, 0, a.status, 44);
     }
@@ -410,8 +448,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     const int m = (warp - 4) >> 2;
     const int r = (warp & 3) * 32 + lane;  // tensor-memory lane = row of tile m
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int hl = r / TT, t = t0 + m * TT + (r % TT);
+    const int hl = r / TT, t = t0 + (SK ? 0 : m) * TT + (r % TT);
     const bool row_ok = hl < gqa && t < a.S;
+    // this tile's key tiles: all (SK = false) or m, m+2, ... (SK)
+    const int my_tiles = SK ? (ntiles > m ? (ntiles - m + 1) / 2 : 0) : ntiles;
     int lim = causal ? n - a.S + t : n - 1;
     lim = min(lim, k_stop - 1);
     const float c = a.scale * 1.4426950408889634f;
@@ -419,11 +459,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     const uint32_t to = tmem + lane_off + 256 + m * 128;
     float m_run = kNegInfTc, l_run = 0.f;
     uint32_t x[32];
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = 0; i < my_tiles; ++i) {
       ok = mbar_wait(&s_full[m], i & 1, a.status, 45);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc::fence_after_sync();
-      const int kbase = k_begin + i * kKT;
+      const int kbase = k_begin + (SK ? 2 * i + m : i) * kKT;
       const bool msk = kbase + kKT - 1 > lim;
       // Fast path: one pass against the running max. Every chunk's max must stay within 2^8
       // of it (one vote per chunk); P stays in registers until all chunks passed, so S is
@@ -565,17 +605,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       if (lane == 0) mbar_arrive(&p_full[m]);
     }
     // ---- epilogue: O row -> output (normalized) or partial row ---------------------------
-    if (ok && ntiles > 0) {
-      ok = mbar_wait(&o_done[m], (ntiles - 1) & 1, a.status, 47);
+    if (ok && my_tiles > 0) {
+      ok = mbar_wait(&o_done[m], (my_tiles - 1) & 1, a.status, 47);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc::fence_after_sync();
       const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
+      const int part = SK ? 2 * split + m : split;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
       for (int qd = 0; qd < 4; ++qd) {
-        if (ntiles > 0) {
+        if (my_tiles > 0) {
           tc::ld32(to + qd * 32, x);
           tc::wait_ld();
         } else {
@@ -593,7 +634,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           }
         if (row_ok) {
           if (P.parts) {
-            float* dst = P.parts + ((long long)split * a.B * a.HQ * a.S + row) * (kD + 4) + qd * 32;
+            float* dst = P.parts + ((long long)part * a.B * a.HQ * a.S + row) * (kD + 4) + qd * 32;
 #pragma unroll
             for (int e = 0; e < 32; e += 4)
               *reinterpret_cast<float4*>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
@@ -609,7 +650,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         }
       }
       if (row_ok && P.parts) {
-        float* dst = P.parts + ((long long)split * a.B * a.HQ * a.S + row) * (kD + 4) + kD;
+        float* dst = P.parts + ((long long)part * a.B * a.HQ * a.S + row) * (kD + 4) + kD;
         *reinterpret_cast<float4*>(dst) = make_float4(m_run, l_run, 0.f, 0.f);
       }
     }
@@ -658,20 +699,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   }
 }
 
-template <typename T, int BITS, int MT>
+template <typename T, int BITS, int MT, bool SK>
 int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {
   using SM = TcSmem<MT>;
   TcParams prm;
   prm.a = a;
   prm.TT = p.tokens_per_tile;
   prm.chunk = p.chunk;
-  const bool direct = combine && p.splits == 1 && a.out_kind == QKV_OUT_NORMALIZED;
+  const bool direct = combine && p.parts == 1 && a.out_kind == QKV_OUT_NORMALIZED;
   // attention calls keep the workspace's leading arrival counters intact (see kCounterBytes)
   prm.parts = direct ? nullptr
                      : reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
                                                 (combine ? kCounterBytes : 0));
   const size_t smem = (size_t)SM::BYTES + 1024;
-  auto kern = prefill_tc_kernel<T, BITS, MT>;
+  auto kern = prefill_tc_kernel<T, BITS, MT, SK>;
   static unsigned attr_done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -686,13 +727,14 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
   if (cudaGetLastError() != cudaSuccess) return QKV_ECUDA;
   if (direct || !combine) return QKV_OK;
   const long long rows = (long long)a.B * a.HQ * a.S;
-  return launch_combine(prm.parts, p.splits, rows, rows, kD, a.out, a.dtype, a.out_kind, st);
+  return launch_combine(prm.parts, p.parts, rows, rows, kD, a.out, a.dtype, a.out_kind, st);
 }
 
 template <typename T, int BITS>
 int launch_tc_mt(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {
-  return p.tiles == 2 ? launch_tc<T, BITS, 2>(a, p, combine, st)
-                      : launch_tc<T, BITS, 1>(a, p, combine, st);
+  // one query tile: both tensor-memory tiles split its keys (see prefill_tc_kernel)
+  return p.tiles == 2 ? launch_tc<T, BITS, 2, false>(a, p, combine, st)
+                      : launch_tc<T, BITS, 2, true>(a, p, combine, st);
 }
 
 }  // namespace
@@ -738,12 +780,13 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
   }
   p.chunk = ((n + best - 1) / best + kKT - 1) / kKT * kKT;
   p.splits = (n + p.chunk - 1) / p.chunk;
+  p.parts = p.splits * (p.tiles == 1 ? 2 : 1);
   return p;
 }
 
 size_t prefill_tc_workspace_bytes(int B, int HQ, int S, int D, const TcPlan& p, bool direct) {
-  if (direct && p.splits == 1) return 0;
-  return kCounterBytes + (size_t)p.splits * B * HQ * S * (D + 4) * sizeof(float);
+  if (direct && p.parts == 1) return 0;
+  return kCounterBytes + (size_t)p.parts * B * HQ * S * (D + 4) * sizeof(float);
 }
 
 int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {

@@ -149,3 +149,19 @@ def test_verify_block_shape(bits):
     q, k, v = make_case(70 + bits, 1, 32, 4, S, 128, n, "bf16", outliers=True)
     c = _cache(k, v, bits, "bf16")
     _check(_run(q, c, n, bits, "bf16", "causal"), _ref(q, k, v, bits, "bf16", n, "causal"))
+
+
+def test_key_split_tiles_partials():
+    """A block that fits one 128-row tile runs its keys on both tensor-memory tiles
+    alternately: each split yields two partial rows per query row."""
+    from chad_b200 import ops
+
+    S, n = 8, 2500 + 8
+    q, k, v = make_case(91, 1, 32, 4, S, 128, n, "bf16", outliers=True)
+    c = _cache(k, v, 4, "bf16")
+    tq = torch_from_f32(q, "bf16")
+    parts = ops.partials(tq, c.keys, c.values, 128 ** -0.5, n, 4, mask="causal", splits=3)
+    assert parts.shape[0] == 6
+    ref = _ref(q, k, v, 4, "bf16", n, "causal")
+    _check(ops.combine(parts.contiguous(), torch.bfloat16), ref)
+    _check(_run(q, c, n, 4, "bf16", "causal", splits=1), ref)
