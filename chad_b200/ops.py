@@ -268,14 +268,17 @@ def combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
 
 def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
             k_quant: Sequence[torch.Tensor], v_quant: Sequence[torch.Tensor], offset: int,
-            bits: int, scale: float, group_size: int = GROUP_SIZE) -> torch.Tensor:
-    """Quantize-append the new chunk at [offset, offset+S) then attend causally over all keys."""
+            bits: int, scale: float, group_size: int = GROUP_SIZE,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Quantize-append the new chunk at [offset, offset+S) then attend causally over all keys
+    (one library call; S = 1 is a decode step)."""
     kw, ks, kb = k_quant
     vw, vs, vb = v_quant
     dev = _need_cuda(q, k_new, v_new, kw)
     B, HQ, S, D = q.shape
     HKV, NP = kw.shape[1], kw.shape[2]
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
     need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size)
     ws = _workspace(dev, need)
     with _on(dev):
