@@ -17,8 +17,9 @@
 //     O_m += P_m V(i) as soon as softmax_m(i) is done and then S_m = Q_m K(i+1)^T, so one
 //     tile's softmax overlaps the other tile's MMAs (ping-pong). MMAs are M=128, N=128, K=16
 //     (N=64 runs at two thirds of the tensor pipe's rate on B200).
-//   * The running max is only raised when it grows by more than 2^8 (log2 units), so the
-//     O rescale in tensor memory is rare; P values stay <= 256.
+//   * The running max is only raised when it grows by more than 2^12, so the O rescale in
+//     tensor memory and the two-pass softmax are rare even on key-outlier data; P values stay
+//     <= 4096 (inside f16 as well as bf16).
 //
 // Dequantized K/V values are round(code * scale + bias) in the 16-bit type with a single
 // rounding (fused multiply-add), the value mx.dequantize returns up to the rare case where
@@ -45,7 +46,7 @@ constexpr int kD = 128;
 constexpr int kKT = 128;         // keys per tile (MMA N of Q K^T)
 constexpr int kWarpsTc = 13;
 constexpr int kThreadsTc = kWarpsTc * 32;
-constexpr float kRescaleLog2 = 8.0f;
+constexpr float kRescaleLog2 = 12.0f;  // P <= 2^12: exact range in bf16 and f16
 constexpr int kPolyPairs = 4;  // > 0: one value pair in kPolyPairs takes exp2_poly2, not the MUFU
 constexpr int kHalf = kKT * 128;       // bytes of one 64-dim half of a K or V tile
 constexpr int kTileBytes = 2 * kHalf;  // one dequantized K or V tile
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       tc::fence_after_sync();
       const int kbase = k_begin + (SK ? 2 * i + m : i) * kKT;
       const bool msk = kbase + kKT - 1 > lim;
-      // Fast path: one pass against the running max. Every chunk's max must stay within 2^8
+      // Fast path: one pass against the running max. Every chunk's max must stay within 2^12
       // of it (one vote per chunk); P stays in registers until all chunks passed, so S is
       // still intact for the two-pass path, which handles the first tile and a new maximum.
       float sa[4] = {0.f, 0.f, 0.f, 0.f};
