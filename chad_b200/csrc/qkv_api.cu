@@ -10,7 +10,6 @@
 #include "../../include/qkv.h"
 #include "qkv_internal.h"
 
-static_assert(qkv::kCounterBytes == QKV_COUNTER_BYTES, "counter area size");
 
 namespace qkv {
 
@@ -236,9 +235,9 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
   const int n_max = std::max(a.n, 1);
   const int R = (HQ / HKV) * S;
   const int rg = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
-  if ((long long)B * HKV * rg > kMaxCounters)
-    return fail(QKV_EUNSUPPORTED, "too many query-row groups (%lld > %d)",
-                (long long)B * HKV * rg, kMaxCounters);
+  if ((long long)HKV * rg > 65535 || B > 65535)
+    return fail(QKV_EUNSUPPORTED, "too many kv heads x query-row groups (%lld) or batch (%d)",
+                (long long)HKV * rg, B);
   decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
   size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
   // (the tensor-core path's running max assumes a positive softmax scale)

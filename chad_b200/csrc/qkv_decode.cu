@@ -157,38 +157,28 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+// Partial rows of the in-kernel merge are stored as (float bits) ^ kPartKey, so that a word
+// reads 0 until its value has landed: kPartKey is a signalling-NaN pattern, and arithmetic
+// only ever produces quiet NaNs, so no stored value encodes to 0. The merger that reads a
+// word writes 0 back; the workspace is zero before the first call and after every call.
+constexpr unsigned kPartKey = 0x7FBADBADu;
 
-
-// Position of output element (query row r, head dim d) in the MMA fragment order the
-// consumer warps publish their accumulators in.
-template <int G, int KS>
-__device__ __forceinline__ int frag_index(int r, int d) {
-  const int nt = r >> 3, rr = r & 7, tq = rr >> 1, ir = rr & 1;
-  const int g = d >> 6, dd = d & 63, gq = dd >> 3, d8 = dd & 7, jj = d8 >> 1, ih = d8 & 1;
-  const int j = g * KS + jj;
-  return ((nt * G * KS + j) * 32 + 4 * gq + tq) * 4 + 2 * ih + ir;
+// Two consecutive floats of a partial row: encoded (merge mode, workspace) or plain
+// (partials handed to the caller).
+__device__ __forceinline__ void store_part(float* dst, float x, float y, int encoded) {
+  if (encoded)
+    __stcg(reinterpret_cast<uint2*>(dst),
+           make_uint2(__float_as_uint(x) ^ kPartKey, __float_as_uint(y) ^ kPartKey));
+  else
+    *reinterpret_cast<float2*>(dst) = make_float2(x, y);
 }
 
 struct DecodeParams {
   AttnArgs a;
   CUtensorMap tmk;  // K codes: (RB bytes, NP, B*HKV)
   CUtensorMap tmv;  // V codes
-  float* gpart;     // per-CTA partial rows [splits][B*HQ*S][D+4]
-  unsigned* counters;  // [kMaxCounters] arrival generations per row group
-  int merge;        // 1: the row group's last CTAs merge the partials into a.out
+  float* gpart;     // per-CTA partial rows [splits][B*HQ*S][D+4], or [..][D+2*D/32] encoded
+  int merge;        // 1: the row group's last splits merge the partials into a.out
 };
 
 template <typename T, int BITS, int D, int NT>
@@ -282,15 +272,17 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   len = min(max(len, 0), a.NP);
   const int p_end = min(p_begin + a.chunk, len);
   const int n_iters = p_end > p_begin ? (p_end - p_begin + kTP - 1) / kTP : 0;
+  // partial rows: [split][B*HQ*S][PW] floats; see store_part for the merge mode's encoding
+  constexpr int kSlices = D / (4 * kMergeCols);
+  const int PW = P.merge ? D + 2 * kSlices : D + 4;
+  const size_t rows_all = (size_t)a.B * a.HQ * a.S;
+  const int nsplit = gridDim.x;
 
   // merge area (reuses the stage ring once the main loop is over)
   float* mw = reinterpret_cast<float*>(smem);  // [kWarps][RG] running max per warp
   float* lw = mw + kWarps * RG;                // [kWarps][RG] sums
   float* ow = lw + kWarps * RG;                // [kWarps][RG*D] outputs, fragment order
-  float* cp = ow + kWarps * RG * D;            // [RG*D] this CTA's output, fragment order
-  float* cm = cp + RG * D;                     // [RG] this CTA's max per row
-  float* cl = cm + RG;                         // [RG] this CTA's sum per row
-  float* xm = cl + RG;                         // merge: [kMergeSlots][kMergeCols] running max
+  float* xm = ow + kWarps * RG * D;            // merge: [kMergeSlots][kMergeCols] running max
   float* xl = xm + kMergeSlots * kMergeCols;   // merge: [kMergeSlots][kMergeCols] sums
   float* xo = xl + kMergeSlots * kMergeCols;   // merge: [kMergeSlots][kMergeCols][4] outputs
 
@@ -727,7 +719,9 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
       }
     }
     named_bar_sync(1, kWarps * 32);
-    float4* co4 = reinterpret_cast<float4*>(cp);
+    // CTA sum of the warps' rows, stored straight into this CTA's partial rows. Fragment
+    // float4 k holds head dims (d0, d0 + 1) of query rows r0 (x, z) and r0 + 1 (y, w).
+    float* gp = P.gpart + ((size_t)split * rows_all + row0 + rbase) * PW;
     for (int k = threadIdx.x; k < RG * D / 4; k += kWarps * 32) {
       float4 acc4 = reinterpret_cast<const float4*>(ow)[k];
 #pragma unroll
@@ -738,9 +732,13 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         acc4.z += x.z;
         acc4.w += x.w;
       }
-      co4[k] = acc4;
+      const int ln = k & 31, t = k >> 5, j = t % (G * KS), nt = t / (G * KS);
+      const int r0 = nt * 8 + 2 * (ln & 3);
+      const int d0 = 64 * (j / KS) + 8 * (ln >> 2) + 2 * (j % KS);
+      if (r0 < rows_here) store_part(gp + (size_t)r0 * PW + d0, acc4.x, acc4.z, P.merge);
+      if (r0 + 1 < rows_here) store_part(gp + (size_t)(r0 + 1) * PW + d0, acc4.y, acc4.w, P.merge);
     }
-    if (threadIdx.x < RG) {
+    if (threadIdx.x < rows_here) {
       const int r = threadIdx.x;
       float mx = mw[r], l = lw[r];
 #pragma unroll
@@ -748,86 +746,83 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         mx = fmaxf(mx, mw[w * RG + r]);
         l += lw[w * RG + r];
       }
-      cm[r] = mx;
-      cl[r] = l;
-    }
-  }
-  __syncthreads();
-
-  // ---- this CTA's partial rows -> workspace; the row group's last CTAs merge them --------
-  const size_t rows_all = (size_t)a.B * a.HQ * a.S;
-  const int nsplit = gridDim.x;
-  {
-    float* gp = P.gpart + ((size_t)split * rows_all + row0 + rbase) * (D + 4);
-    for (int e = threadIdx.x; e < rows_here * D; e += kThreads) {
-      const int r = e / D, d = e - r * D;
-      gp[(size_t)r * (D + 4) + d] = cp[frag_index<G, KS>(r, d)];
-    }
-    if (threadIdx.x < rows_here) {
-      gp[(size_t)threadIdx.x * (D + 4) + D] = cm[threadIdx.x];
-      gp[(size_t)threadIdx.x * (D + 4) + D + 1] = cl[threadIdx.x];
-    }
-  }
-  if (!P.merge) return;
-  // Arrival ticket (acq_rel at gpu scope: this CTA's rows, ordered before it by the barrier,
-  // are visible to whoever sees the count). The row group's counter advances by exactly
-  // 1024 per call: one per CTA, and the last arrival adds the rest, so the low 10 bits
-  // are this call's ticket and nothing needs resetting. The last `nm` arrivals merge one
-  // (row, 32-dim slice) unit each once the generation is complete; every CTA of the row
-  // group is resident before any of them waits (one wave, dispatched in order).
-  __syncthreads();
-  __shared__ unsigned s_ticket;
-  const int grp = blockIdx.z * gridDim.y + blockIdx.y;  // (b, kv head, row group)
-  unsigned* arrive = P.counters + grp;
-  if (threadIdx.x == 0) {
-    const unsigned old = atom_add_acq_rel(arrive, 1u);
-    if ((old & 1023u) == (unsigned)nsplit - 1u) red_add_release(arrive, 1024u - (unsigned)nsplit);
-    s_ticket = old;
-  }
-  __syncthreads();
-  constexpr int kSlices = D / (4 * kMergeCols);
-  const int units = kSlices * rows_here;
-  const int nm = min(nsplit, units);
-  const unsigned base = s_ticket & ~1023u;
-  const int ticket = (int)(s_ticket & 1023u);
-  if (ticket < nsplit - nm) return;
-  if (threadIdx.x == 0) {
-    bool ok = ld_acquire(arrive) - base >= 1024u;
-    const unsigned long long t0 = ok ? 0ull : global_ns();
-    while (!ok) {
-      __nanosleep(64);
-      ok = ld_acquire(arrive) - base >= 1024u;
-      if (!ok && global_ns() - t0 > kSpinNanos) {
-        flag_device_error(a.status, 14);
-        break;
+      if (P.merge) {
+#pragma unroll
+        for (int s = 0; s < kSlices; ++s) store_part(gp + (size_t)r * PW + D + 2 * s, mx, l, 1);
+      } else {
+        store_part(gp + (size_t)r * PW + D, mx, l, 0);
       }
     }
   }
-  __syncthreads();
+  // ---- the row group's last `nm` splits merge the partials, one (row, 32-dim slice) unit
+  // each. Every other CTA is done once its stores are issued. A merger polls the words it
+  // needs until none reads as "not written" (0), then zeroes them for the next call. Those
+  // splits are dispatched after the rest of their row group, so nothing they wait for
+  // still needs a slot.
+  if (!P.merge) return;
+  const int units = kSlices * rows_here;
+  const int nm = min(nsplit, units);
+  const int first = nsplit - nm;
+  if (split < first) return;
   const int q4 = threadIdx.x % kMergeCols, slot = threadIdx.x / kMergeCols;  // columns x slots
   static_assert(kThreads % kMergeCols == 0 && D % (4 * kMergeCols) == 0, "merge layout");
-  for (int u = ticket - (nsplit - nm); u < units; u += nm) {
+  static_assert(kMergeCols == 8 && 32 % kMergeCols == 0, "a slot's threads share one warp");
+  for (int u = split - first; u < units; u += nm) {
     const int r = u / kSlices, sl = u - r * kSlices;
     const size_t rowi = row0 + rbase + r;
     float mt = kNegInf, lt = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     {
-      // this thread's partials: p = slot, slot + kMergeSlots, ... in batches of 8 (online)
-      for (int p0 = slot; p0 < nsplit; p0 += 8 * kMergeSlots) {
+      // this thread's partials: p = slot, slot + kMergeSlots, ... in batches of 8 (online).
+      // Every thread runs every batch (a slot past the last split just has nothing to
+      // load), so the warp votes in the poll below always see all 32 lanes.
+      for (int b0 = 0; b0 < nsplit; b0 += 8 * kMergeSlots) {
+        const int p0 = b0 + slot;
         float pm[8], pl[8];
         float4 po[8];
+        unsigned need = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const int p = p0 + k * kMergeSlots;
-          if (p < nsplit) {
-            const float* src = P.gpart + ((size_t)p * rows_all + rowi) * (D + 4);
-            pm[k] = __ldcg(src + D);
-            pl[k] = __ldcg(src + D + 1);
-            po[k] = __ldcg(reinterpret_cast<const float4*>(src + sl * 4 * kMergeCols) + q4);
-          } else {
-            pm[k] = kNegInf;
-            pl[k] = 0.f;
-            po[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          pm[k] = kNegInf;
+          pl[k] = 0.f;
+          po[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (p0 + k * kMergeSlots < nsplit) need |= 1u << k;
+        }
+        const unsigned want = need;
+        unsigned long long t0 = 0;
+        for (;;) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (need & (1u << k)) {
+              const float* src =
+                  P.gpart + ((size_t)(p0 + k * kMergeSlots) * rows_all + rowi) * PW;
+              const uint2 ml = __ldcg(reinterpret_cast<const uint2*>(src + D + 2 * sl));
+              const uint4 o4 = __ldcg(reinterpret_cast<const uint4*>(src + sl * 4 * kMergeCols) + q4);
+              if (ml.x && ml.y && o4.x && o4.y && o4.z && o4.w) {
+                need &= ~(1u << k);
+                pm[k] = __uint_as_float(ml.x ^ kPartKey);
+                pl[k] = __uint_as_float(ml.y ^ kPartKey);
+                po[k] = make_float4(__uint_as_float(o4.x ^ kPartKey), __uint_as_float(o4.y ^ kPartKey),
+                                    __uint_as_float(o4.z ^ kPartKey), __uint_as_float(o4.w ^ kPartKey));
+              }
+            }
+          }
+          if (!__any_sync(0xffffffffu, need)) break;
+          const unsigned long long now = global_ns();
+          if (t0 == 0) t0 = now;
+          if (__any_sync(0xffffffffu, now - t0 > kSpinNanos)) {  // (one verdict per warp)
+            flag_device_error(a.status, 14);
+            break;
+          }
+          __nanosleep(32);
+        }
+        // every lane of the slot holds its words: hand them back as "not written"
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (want & (1u << k)) {
+            float* src = P.gpart + ((size_t)(p0 + k * kMergeSlots) * rows_all + rowi) * PW;
+            __stcg(reinterpret_cast<uint4*>(src + sl * 4 * kMergeCols) + q4, make_uint4(0u, 0u, 0u, 0u));
+            if (q4 == 0) __stcg(reinterpret_cast<uint2*>(src + D + 2 * sl), make_uint2(0u, 0u));
           }
         }
         float mx = mt;
@@ -898,8 +893,8 @@ constexpr int kCombineBatch = 8;
 
 template <typename TO, int D>
 __global__ void __launch_bounds__(kCombineWarps * 32)
-    combine_kernel(const float* __restrict__ parts, int n_parts, long long part_stride_rows,
-                   long long rows, TO* __restrict__ out, float* __restrict__ out_part) {
+    combine_kernel(const float* parts, int n_parts, long long part_stride_rows, long long rows,
+                   TO* __restrict__ out, float* __restrict__ out_part, float* clear) {
   constexpr int E = D / 32;
   __shared__ float red[kCombineWarps][D];
   __shared__ float wmax[kCombineWarps], wsum[kCombineWarps];
@@ -930,6 +925,19 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
         pl[k] = 0.f;
 #pragma unroll
         for (int e = 0; e < E; ++e) po[k][e] = 0.f;
+      }
+    }
+    if (clear) {  // partials in an attention workspace: leave the words read as zero
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < kCombineBatch; ++k) {
+        const int p = p0 + warp + k * kCombineWarps;
+        if (p < n_parts) {
+          float* pr = clear + row * (D + 4) + p * pstride;
+#pragma unroll
+          for (int e = 0; e < E; ++e) pr[lane * E + e] = 0.f;
+          if (lane == 0) *reinterpret_cast<float2*>(pr + D) = make_float2(0.f, 0.f);
+        }
       }
     }
     float mx = pm[0];
@@ -1012,8 +1020,7 @@ bool make_code_map(CUtensorMap* m, const void* base, int NP, long long bhs) {
 template <int D, int NT>
 constexpr size_t merge_bytes() {
   constexpr int RG = 8 * NT;
-  return ((size_t)kWarps * RG * 2 + (size_t)kWarps * RG * D + (size_t)RG * D + 2 * RG +
-          (size_t)kMergeSlots * kMergeCols * 6) *
+  return ((size_t)kWarps * RG * 2 + (size_t)kWarps * RG * D + (size_t)kMergeSlots * kMergeCols * 6) *
          4;
 }
 
@@ -1029,9 +1036,7 @@ int launch_split(const AttnArgs& a, bool merge, cudaStream_t st) {
   DecodeParams p;
   p.a = a;
   p.merge = merge ? 1 : 0;
-  p.counters = reinterpret_cast<unsigned*>(a.workspace);
-  p.gpart = reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
-                                     (merge ? kCounterBytes : 0));
+  p.gpart = reinterpret_cast<float*>(a.workspace);
   if (!make_code_map<BITS, D>(&p.tmk, a.kw, a.NP, (long long)a.B * a.HKV) ||
       !make_code_map<BITS, D>(&p.tmv, a.vw, a.NP, (long long)a.B * a.HKV))
     return QKV_ECUDA;
@@ -1163,7 +1168,9 @@ size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluste
 
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster) {
   (void)HKV;
-  return kCounterBytes + decode_partials_bytes(B, HQ, S, D, splits, cluster);
+  (void)cluster;
+  // encoded partial rows: D values and one (max, sum) pair per 32-dim merge slice
+  return (size_t)splits * B * HQ * S * (D + 2 * (D / 32)) * sizeof(float);
 }
 
 int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, false, st); }
@@ -1171,11 +1178,12 @@ int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_
 int launch_decode(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, true, st); }
 
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
-                   int D, void* out, int out_dtype, int out_kind, cudaStream_t st) {
+                   int D, void* out, int out_dtype, int out_kind, cudaStream_t st, bool clear) {
   if (rows == 0) return QKV_OK;
   const int warps = kCombineWarps;
   const unsigned grid = (unsigned)rows;
   float* op = out_kind == QKV_OUT_PARTIAL ? (float*)out : nullptr;
+  float* cl = clear ? const_cast<float*>(parts) : nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(warps * 32, 1, 1);
@@ -1190,10 +1198,10 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
   case DD:                                                                                   \
     if (out_dtype == QKV_BF16)                                                               \
       e = cudaLaunchKernelEx(&cfg, combine_kernel<__nv_bfloat16, DD>, parts, n_parts,        \
-                             part_stride_rows, rows, (__nv_bfloat16*)out, op);               \
+                             part_stride_rows, rows, (__nv_bfloat16*)out, op, cl);           \
     else                                                                                     \
       e = cudaLaunchKernelEx(&cfg, combine_kernel<__half, DD>, parts, n_parts,               \
-                             part_stride_rows, rows, (__half*)out, op);                      \
+                             part_stride_rows, rows, (__half*)out, op, cl);                  \
     break;
   switch (D) {
     QKV_C_CASE(64)

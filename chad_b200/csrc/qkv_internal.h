@@ -54,12 +54,8 @@ struct AttnArgs {
 };
 
 // Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
-// Upper bound on (batch x kv heads x query-row groups) per call.
-constexpr int kMaxCounters = 16384;
-// Attention calls keep kMaxCounters arrival counters (and room for as many more) at the
-// start of the workspace: zero before the first call; each call advances a row group's
-// counter by a whole 1024 (it is never reset). Partial rows follow.
-constexpr size_t kCounterBytes = 2 * kMaxCounters * sizeof(unsigned);
+// The attention workspace holds partial rows whose words read 0 until written; it is zero
+// before the first call and every call leaves it zero (the readers clear what they read).
 int decode_rows_per_group(int R, int D);    // query rows handled by one CTA (8 or 16)
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster);
 size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster);
@@ -73,8 +69,10 @@ inline int decode_ctas_per_sm(int R, int D, int bits) {
 int launch_decode(const AttnArgs& a, cudaStream_t st);  // split kernel + combine
 int launch_split_only(const AttnArgs& a, cudaStream_t st);  // partial rows into a.workspace
 
+// clear: the partials are in an attention workspace; zero every word read
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
-                   int D, void* out, int out_dtype, int out_kind, cudaStream_t st);
+                   int D, void* out, int out_dtype, int out_kind, cudaStream_t st,
+                   bool clear = false);
 
 int launch_quantize(const void* x, int x_dtype, void* w, void* sc, void* bi, int B, int H,
                     int S, int D, int NP, int offset, int bits, int scale_dtype,

@@ -14,11 +14,11 @@
 // array's name to a kernel, since in host code that name is only a stand-in, not a device
 // address. Make that first call on a device before any stream capture begins.
 //
-// Sharing: every call on a device uses the same array, which keeps the last call's contents.
-// Each call writes every partial row before reading it. The array's first 128 KiB hold the
-// per-row-group arrival counters of the attention kernel's merge: they start at zero (static
-// storage is zero-initialized) and every call returns them to zero. Two calls whose kernels
-// overlap on the GPU (for example on two streams at once) race on the array: serialize them.
+// Sharing: every call on a device uses the same array. The attention kernel's merge reads a
+// partial-row word as "not yet written" while it is zero and zeroes every word it reads, so
+// the array starts at zero (static storage is zero-initialized) and every call returns it to
+// zero. Two calls whose kernels overlap on the GPU (for example on two streams at once) race
+// on the array: serialize them.
 #include <algorithm>
 
 #include "../../include/qkv.h"

@@ -708,10 +708,7 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
   prm.TT = p.tokens_per_tile;
   prm.chunk = p.chunk;
   const bool direct = combine && p.parts == 1 && a.out_kind == QKV_OUT_NORMALIZED;
-  // attention calls keep the workspace's leading arrival counters intact (see kCounterBytes)
-  prm.parts = direct ? nullptr
-                     : reinterpret_cast<float*>(reinterpret_cast<char*>(a.workspace) +
-                                                (combine ? kCounterBytes : 0));
+  prm.parts = direct ? nullptr : reinterpret_cast<float*>(a.workspace);
   const size_t smem = (size_t)SM::BYTES + 1024;
   auto kern = prefill_tc_kernel<T, BITS, MT, SK>;
   static unsigned attr_done = 0;
@@ -728,7 +725,9 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
   if (cudaGetLastError() != cudaSuccess) return QKV_ECUDA;
   if (direct || !combine) return QKV_OK;
   const long long rows = (long long)a.B * a.HQ * a.S;
-  return launch_combine(prm.parts, p.parts, rows, rows, kD, a.out, a.dtype, a.out_kind, st);
+  // the partials sit in the attention workspace: the combine clears what it reads
+  return launch_combine(prm.parts, p.parts, rows, rows, kD, a.out, a.dtype, a.out_kind, st,
+                        true);
 }
 
 template <typename T, int BITS>
@@ -787,7 +786,7 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
 
 size_t prefill_tc_workspace_bytes(int B, int HQ, int S, int D, const TcPlan& p, bool direct) {
   if (direct && p.parts == 1) return 0;
-  return kCounterBytes + (size_t)p.parts * B * HQ * S * (D + 4) * sizeof(float);
+  return (size_t)p.parts * B * HQ * S * (D + 4) * sizeof(float);
 }
 
 int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st) {

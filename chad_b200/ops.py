@@ -139,8 +139,8 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     key = (dev.type, dev.index)
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
-        # zeroed once: the leading arrival counters must start at zero (every call leaves
-        # them zero again)
+        # zeroed once: the in-kernel merge reads a zero word as "not yet written" (every
+        # call leaves the workspace zero again)
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
         _WS[key] = ws
     return ws

@@ -90,11 +90,11 @@ int qkv_dequantize(const void* w, const void* scales, const void* biases, void* 
 
 /*
  * Bytes of scratch that qkv_attention needs for these sizes (n_max = largest key count).
- * The workspace's first QKV_COUNTER_BYTES bytes hold arrival counters of the in-kernel
- * merge: zero them once before the first call (cudaMemset); every call leaves them zero.
- * One workspace serves one stream at a time.
+ * The in-kernel merge reads a zero word of the workspace as "not yet written": zero the
+ * whole workspace once before the first call (cudaMemset); every call leaves it zero again.
+ * After a call reports a device error (QKV_EDEVICE), zero it again. One workspace serves
+ * one stream at a time.
  */
-#define QKV_COUNTER_BYTES 131072
 size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int bits,
                           int group_size);
 
@@ -117,8 +117,7 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
  *             count); a stride of 0 broadcasts
  *   splits:   split count along the keys (0 = choose from the SM count)
  *   workspace: >= qkv_workspace_size(B, HQ, HKV, S, D, max key count, bits, group_size),
- *             its first QKV_COUNTER_BYTES zeroed before the first call (left zero by every
- *             call)
+ *             all zero before the first call (every call leaves it zero)
  */
 int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
                   const void* vw, const void* vs, const void* vb, void* out,
