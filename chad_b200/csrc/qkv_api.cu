@@ -157,6 +157,10 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
   int splits = 1, chunk = 16, cluster = 1;
   decode_plan(B, HQ, HKV, S, D, bits, std::max(n_max, 1), 0, &splits, &chunk, &cluster);
   size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, splits, cluster);
+  // ragged batches (per-batch lengths) share the CTAs by key count
+  if (B > 1)
+    need = std::max(need, decode_balanced_bytes(B, HQ, S, D,
+                                                decode_plan_balanced(B, HQ, HKV, S, D, bits)));
   // multi-token calls may take the tensor-core path: room for its split partials too
   if (prefill_tc_eligible(B, HQ, HKV, S, D, nullptr, nullptr, nullptr, QKV_MASK_CAUSAL)) {
     const TcPlan tp = prefill_tc_plan(B, HQ, HKV, S, std::max(n_max, 1), 0);
@@ -174,7 +178,7 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
                const int* total_lens, int bits, int group_size, int dtype, float scale,
                int mask_kind, const void* mask, int mask_nk, long long mask_sb,
                long long mask_sh, long long mask_sq, int splits, void* workspace,
-               size_t ws_bytes, bool direct) {
+               size_t ws_bytes, bool direct, bool merge) {
   int rc = check_cache_shape(D, bits, group_size);
   if (rc) return rc;
   if (!q || !kw || !ks || !kb || !vw || !vs || !vb || !out)
@@ -240,6 +244,12 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
                 (long long)HKV * rg, B);
   decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
   size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
+  if (merge && lens && B > 1 && splits == 0) {
+    // ragged batches: share the CTAs by key count instead of splitting every batch alike
+    a.balanced = decode_plan_balanced(B, HQ, HKV, S, D, bits);
+    a.splits = a.balanced + B;
+    need = decode_balanced_bytes(B, HQ, S, D, a.balanced);
+  }
   // (the tensor-core path's running max assumes a positive softmax scale)
   a.use_tc = prefill_tc_eligible(B, HQ, HKV, S, D, lens, pos_base, total_lens, a.mask_kind) &&
              scale > 0.f;
@@ -270,7 +280,7 @@ int qkv_attention(const void* q, const void* kw, const void* ks, const void* kb,
   int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, n, lens,
                       pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
                       mask_nk, mask_sb, mask_sh, mask_sq, splits, workspace, ws_bytes,
-                      out_kind == QKV_OUT_NORMALIZED);
+                      out_kind == QKV_OUT_NORMALIZED, true);
   if (rc) return rc;
   a.out_kind = out_kind;
   rc = a.use_tc ? launch_prefill_tc(a, a.tc, true, static_cast<cudaStream_t>(stream))
@@ -290,7 +300,8 @@ int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, 
   AttnArgs a;
   int rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, parts, B, HQ, HKV, S, D, NP, n, lens,
                       pos_base, total_lens, bits, group_size, dtype, scale, mask_kind, mask,
-                      mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes, false);
+                      mask_nk, mask_sb, mask_sh, mask_sq, splits, parts, parts_bytes, false,
+                      false);
   if (rc) return rc;
   a.out_kind = QKV_OUT_PARTIAL;
   *n_parts = a.use_tc ? a.tc.parts : a.splits / a.cluster;

@@ -201,10 +201,10 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   // wait for griddepcontrol.wait below; only the producer's first stages of cache positions
   // below a.prefetch_limit (older than the tokens appended by the predecessor) go earlier.
   asm volatile("griddepcontrol.launch_dependents;");
-  const int split = blockIdx.x;
+  int split = blockIdx.x;  // (balanced mode: batch and split follow from the lengths below)
   const int hkv = blockIdx.y % a.HKV;
   const int rg = blockIdx.y / a.HKV;
-  const int b = blockIdx.z;
+  int b = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;  // MMA group id
@@ -212,9 +212,10 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
 
   const int gqa = a.HQ / a.HKV;
   const int R = gqa * a.S;  // query rows sharing this kv head
-  const int p_begin = split * a.chunk;
-  const long long bh = (long long)b * a.HKV + hkv;
-  const long long row0 = ((long long)b * a.HQ + (long long)hkv * gqa) * a.S;  // first q row
+  int chunk = a.chunk;
+  int p_begin = split * chunk;
+  long long bh = (long long)b * a.HKV + hkv;
+  long long row0 = ((long long)b * a.HQ + (long long)hkv * gqa) * a.S;  // first q row
   const int rbase = rg * RG;
   const int rows_here = min(RG, R - rbase);
 
@@ -268,15 +269,46 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
       issue_stage(pre++);
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  int nsplit = gridDim.x;  // splits of this CTA's batch
+  int pset = 0;            // partial set of the batch's split 0
+  if (a.balanced) {
+    // Ragged lengths: the gridDim.x CTAs of a (kv head, row group) are shared by all batches
+    // in proportion to their key counts. chunk = total keys / a.balanced, rounded up to whole
+    // stages; batch b takes max(1, ceil(len_b / chunk)) consecutive CTAs, which sum to at
+    // most a.balanced + B = gridDim.x. Lengths are read only after the dependency wait.
+    long long total = 0;
+    for (int bb = 0; bb < a.B; ++bb) total += min(max(a.lens[bb], 0), a.NP);
+    const long long per = (total + a.balanced - 1) / a.balanced;
+    chunk = (int)max((long long)kTP, (per + kTP - 1) / kTP * kTP);
+    int first_cta = 0;
+    b = -1;
+    for (int bb = 0; bb < a.B; ++bb) {
+      const int lb = min(max(a.lens[bb], 0), a.NP);
+      const int cb = max(1, (lb + chunk - 1) / chunk);
+      if (b < 0 && (int)blockIdx.x < first_cta + cb) {
+        b = bb;
+        split = blockIdx.x - first_cta;
+        nsplit = cb;
+        pset = first_cta;
+      }
+      first_cta += cb;
+    }
+    if (b < 0) return;  // a spare CTA: every batch is covered (uniform across the CTA)
+    p_begin = split * chunk;
+    bh = (long long)b * a.HKV + hkv;
+    row0 = ((long long)b * a.HQ + (long long)hkv * gqa) * a.S;
+  }
   int len = a.lens ? a.lens[b] : a.n;
   len = min(max(len, 0), a.NP);
-  const int p_end = min(p_begin + a.chunk, len);
+  const int p_end = min(p_begin + chunk, len);
   const int n_iters = p_end > p_begin ? (p_end - p_begin + kTP - 1) / kTP : 0;
-  // partial rows: [split][B*HQ*S][PW] floats; see store_part for the merge mode's encoding
+  // Partial rows: [set][rows][PW] floats, see store_part for the merge mode's encoding. A
+  // set is one split of all batches (rows = B*HQ*S), or in balanced mode one CTA of one
+  // batch (rows = HQ*S, the batch's splits are sets pset .. pset + nsplit - 1).
   constexpr int kSlices = D / (4 * kMergeCols);
   const int PW = P.merge ? D + 2 * kSlices : D + 4;
-  const size_t rows_all = (size_t)a.B * a.HQ * a.S;
-  const int nsplit = gridDim.x;
+  const size_t prows = a.balanced ? (size_t)a.HQ * a.S : (size_t)a.B * a.HQ * a.S;
+  const long long prow0 = a.balanced ? (long long)hkv * gqa * a.S : row0;  // row0 within a set
 
   // merge area (reuses the stage ring once the main loop is over)
   float* mw = reinterpret_cast<float*>(smem);  // [kWarps][RG] running max per warp
@@ -721,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     named_bar_sync(1, kWarps * 32);
     // CTA sum of the warps' rows, stored straight into this CTA's partial rows. Fragment
     // float4 k holds head dims (d0, d0 + 1) of query rows r0 (x, z) and r0 + 1 (y, w).
-    float* gp = P.gpart + ((size_t)split * rows_all + row0 + rbase) * PW;
+    float* gp = P.gpart + ((size_t)(pset + split) * prows + prow0 + rbase) * PW;
     for (int k = threadIdx.x; k < RG * D / 4; k += kWarps * 32) {
       float4 acc4 = reinterpret_cast<const float4*>(ow)[k];
 #pragma unroll
@@ -764,12 +796,16 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   const int nm = min(nsplit, units);
   const int first = nsplit - nm;
   if (split < first) return;
+  // the merge scratch reuses the stage ring: no thread (the producer warp's lanes included,
+  // which may have nothing to poll) writes it before every consumer is done with the ring
+  __syncthreads();
   const int q4 = threadIdx.x % kMergeCols, slot = threadIdx.x / kMergeCols;  // columns x slots
   static_assert(kThreads % kMergeCols == 0 && D % (4 * kMergeCols) == 0, "merge layout");
   static_assert(kMergeCols == 8 && 32 % kMergeCols == 0, "a slot's threads share one warp");
   for (int u = split - first; u < units; u += nm) {
     const int r = u / kSlices, sl = u - r * kSlices;
-    const size_t rowi = row0 + rbase + r;
+    const size_t rowi = row0 + rbase + r;   // output row
+    const size_t prowi = prow0 + rbase + r;  // row within a partial set
     float mt = kNegInf, lt = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     {
@@ -795,7 +831,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
           for (int k = 0; k < 8; ++k) {
             if (need & (1u << k)) {
               const float* src =
-                  P.gpart + ((size_t)(p0 + k * kMergeSlots) * rows_all + rowi) * PW;
+                  P.gpart + ((size_t)(pset + p0 + k * kMergeSlots) * prows + prowi) * PW;
               const uint2 ml = __ldcg(reinterpret_cast<const uint2*>(src + D + 2 * sl));
               const uint4 o4 = __ldcg(reinterpret_cast<const uint4*>(src + sl * 4 * kMergeCols) + q4);
               if (ml.x && ml.y && o4.x && o4.y && o4.z && o4.w) {
@@ -820,7 +856,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if (want & (1u << k)) {
-            float* src = P.gpart + ((size_t)(p0 + k * kMergeSlots) * rows_all + rowi) * PW;
+            float* src = P.gpart + ((size_t)(pset + p0 + k * kMergeSlots) * prows + prowi) * PW;
             __stcg(reinterpret_cast<uint4*>(src + sl * 4 * kMergeCols) + q4, make_uint4(0u, 0u, 0u, 0u));
             if (q4 == 0) __stcg(reinterpret_cast<uint2*>(src + D + 2 * sl), make_uint2(0u, 0u));
           }
@@ -1051,7 +1087,7 @@ int launch_split(const AttnArgs& a, bool merge, cudaStream_t st) {
     attr_done |= 1u << (dev & 31);
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.splits, a.HKV * row_groups, a.B);
+  cfg.gridDim = dim3(a.splits, a.HKV * row_groups, a.balanced ? 1 : a.B);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -1164,6 +1200,20 @@ void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int 
 size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster) {
   (void)cluster;
   return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
+}
+
+int decode_plan_balanced(int B, int HQ, int HKV, int S, int D, int bits) {
+  const int R = (HQ / HKV) * S;
+  const int rgs = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
+  const int cols = std::max(1, HKV * rgs);
+  int slots = max_ctas_any(bits, D, R);
+  if (slots <= 0) slots = decode_ctas_per_sm(R, D, bits) * num_sms();
+  // one wave: balanced + B CTAs per column; a batch's split count stays below kMaxSplits
+  return std::max(1, std::min(slots / cols - B, kMaxSplits - 1));
+}
+
+size_t decode_balanced_bytes(int B, int HQ, int S, int D, int balanced) {
+  return (size_t)(balanced + B) * HQ * S * (D + 2 * (D / 32)) * sizeof(float);
 }
 
 size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster) {

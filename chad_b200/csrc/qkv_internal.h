@@ -44,6 +44,8 @@ struct AttnArgs {
   int splits;   // resolved split count (>= 1, a multiple of cluster)
   int chunk;    // keys per split (multiple of the 16-key warp tile)
   int cluster;  // CTAs per thread-block cluster along the splits (1..8)
+  int balanced; // > 0 (ragged lens, merged in-kernel): the splits CTAs of a (kv head, row
+                // group) are shared by the batches by key count, chunk = total / balanced
   void* workspace;
   size_t ws_bytes;
   int* status;  // device status word for bounded-wait failures
@@ -61,6 +63,10 @@ size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, 
 size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster);
 void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want_splits,
                  int* splits, int* chunk, int* cluster);
+// Ragged batches merged in-kernel: CTAs per (kv head, row group) shared by the batches
+// (= balanced + B); returns balanced. The workspace need is decode_balanced_bytes.
+int decode_plan_balanced(int B, int HQ, int HKV, int S, int D, int bits);
+size_t decode_balanced_bytes(int B, int HQ, int S, int D, int balanced);
 // resident CTAs per SM the decode kernel is built for (register budget per instantiation)
 inline int decode_ctas_per_sm(int R, int D, int bits) {
   return (R <= 8 && D <= 128 && bits == 8) ? 3 : 2;

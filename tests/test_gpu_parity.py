@@ -212,6 +212,45 @@ def test_ragged_lengths_and_partials_combine():
     assert np.abs(f32_of(merged) - ref).max() < 2e-2
 
 
+@pytest.mark.parametrize("lens,bits,S", [
+    ([5000, 0, 1, 4096], 4, 1),       # an empty batch and a one-key batch
+    ([3000, 3000, 3000, 3000, 3000, 3000], 8, 1),
+    ([64, 8191, 200, 7000, 1, 4500, 33, 128], 4, 1),
+    ([2500, 700, 4100], 8, 3),        # multi-token rows (causal) over ragged lengths
+])
+def test_ragged_lengths_balanced_against_oracle(lens, bits, S):
+    """Ragged batches share the CTAs by key count (the in-kernel merge's balanced mode):
+    every batch, including empty and one-key ones, against the oracle, and against the
+    per-batch split mode (forced split count) on the same inputs."""
+    from chad_b200 import ops
+
+    B, HQ, HKV, D = len(lens), 16, 2, 128
+    NP = (max(lens) + 255) // 256 * 256
+    lens = np.array(lens, np.int32)
+    q, k, v = make_case(77 + B + bits, B, HQ, HKV, S, D, NP, "bf16", outliers=True)
+    c = _cache(k, v, bits, "bf16")
+    tq = torch_from_f32(q, "bf16")
+    tl = torch.from_numpy(lens).cuda()
+    mask = "causal" if S > 1 else None
+    out = ops.attention(tq, c.keys, c.values, D ** -0.5, NP, bits, lens=tl, mask=mask)
+    kq, vq = _oracle_quant(k, bits, "bf16"), _oracle_quant(v, bits, "bf16")
+    live = lens > 0  # a batch with no keys has no softmax: its rows come out zero
+
+    def sel(t):
+        return tuple(x[live] for x in t)
+
+    ref = orc.attention_quantized_fp32(q[live], sel(kq), sel(vq), D ** -0.5, lens[live], bits,
+                                       64, _np_mask(mask), "bf16")
+    got = f32_of(out)
+    assert np.isfinite(got).all()
+    assert (got[~live] == 0).all()
+    err = np.abs(got[live] - ref)
+    assert err.max() < 2e-2 and err.mean() < 2e-3
+    dense = ops.attention(tq, c.keys, c.values, D ** -0.5, NP, bits, lens=tl, mask=mask,
+                          splits=5)
+    assert np.abs(f32_of(dense)[live] - got[live]).max() < 2e-2
+
+
 def test_prefill_chunk_over_prefix():
     """Prefix cache + new chunk quantized on append, causal within the chunk."""
     from chad_b200 import ops
