@@ -111,9 +111,10 @@ int qkv_device_status(void* stream, int reset) {
   return v;
 }
 
-int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void* biases, int B,
-                        int H, int S, int D, int NP, int offset, int bits, int group_size,
-                        int scale_dtype, void* stream) {
+namespace {
+int check_append(const void* x, int x_dtype, const void* w, const void* scales,
+                 const void* biases, int B, int H, int S, int D, int NP, int offset, int bits,
+                 int group_size, int scale_dtype) {
   int rc = check_cache_shape(D, bits, group_size);
   if (rc) return rc;
   if (!x || !w || !scales || !biases) return fail(QKV_EINVAL, "null pointer");
@@ -125,6 +126,16 @@ int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void*
     return fail(QKV_EINVAL, "bad x_dtype %d", x_dtype);
   if (scale_dtype != QKV_BF16 && scale_dtype != QKV_F16)
     return fail(QKV_EINVAL, "bad scale_dtype %d", scale_dtype);
+  return QKV_OK;
+}
+}  // namespace
+
+int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void* biases, int B,
+                        int H, int S, int D, int NP, int offset, int bits, int group_size,
+                        int scale_dtype, void* stream) {
+  int rc = check_append(x, x_dtype, w, scales, biases, B, H, S, D, NP, offset, bits, group_size,
+                        scale_dtype);
+  if (rc) return rc;
   rc = launch_quantize(x, x_dtype, w, scales, biases, B, H, S, D, NP, offset, bits, scale_dtype,
                        static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "quantize: unsupported shape");
@@ -331,11 +342,20 @@ int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, v
                 int NP, int offset, int bits, int group_size, int dtype, float scale,
                 void* workspace, size_t ws_bytes, void* stream) {
   if (!k_new || !v_new) return fail(QKV_EINVAL, "null new-token K/V");
-  int rc = qkv_quantize_append(k_new, dtype, kw, ks, kb, B, HKV, S, D, NP, offset, bits,
-                               group_size, dtype, stream);
+  int rc = check_append(k_new, dtype, kw, ks, kb, B, HKV, S, D, NP, offset, bits, group_size,
+                        dtype);
   if (rc) return rc;
-  rc = qkv_quantize_append(v_new, dtype, vw, vs, vb, B, HKV, S, D, NP, offset, bits, group_size,
-                           dtype, stream);
+  rc = check_append(v_new, dtype, vw, vs, vb, B, HKV, S, D, NP, offset, bits, group_size, dtype);
+  if (rc) return rc;
+  // K and V of the new tokens in one launch
+  const void* xs[2] = {k_new, v_new};
+  void* ws_[2] = {kw, vw};
+  void* ss[2] = {ks, vs};
+  void* bs[2] = {kb, vb};
+  rc = launch_quantize_jobs(xs, dtype, ws_, ss, bs, 2, B, HKV, S, D, NP, offset, bits, dtype,
+                            static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "quantize: unsupported shape");
+  rc = cuda_check("qkv_prefill append");
   if (rc) return rc;
   return qkv_attention(q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, offset + S, nullptr,
                        nullptr, nullptr, bits, group_size, dtype, scale, QKV_MASK_CAUSAL, nullptr,

@@ -80,6 +80,10 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
                    int D, void* out, int out_dtype, int out_kind, cudaStream_t st,
                    bool clear = false);
 
+// up to two tensors (K and V of one append) quantized by one launch
+int launch_quantize_jobs(const void* const* x, int x_dtype, void* const* w, void* const* sc,
+                         void* const* bi, int jobs, int B, int H, int S, int D, int NP,
+                         int offset, int bits, int scale_dtype, cudaStream_t st);
 int launch_quantize(const void* x, int x_dtype, void* w, void* sc, void* bi, int B, int H,
                     int S, int D, int NP, int offset, int bits, int scale_dtype,
                     cudaStream_t st);

@@ -247,6 +247,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   __shared__ uint32_t tmem_sh;
 
   const AttnArgs& a = P.a;
+  // Programmatic dependent launch: the next kernel may be scheduled once every CTA of this
+  // one has started; this one touches no global memory before griddepcontrol.wait below.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int TT = P.TT;
   const int gqa = a.HQ / a.HKV;
@@ -305,6 +308,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       vbi = ldg4((const uint8_t*)a.vb + sc0 + (long long)key * 4);
     }
   };
+  // barriers and tensor memory are set up; q, the cache (its newest positions may come from
+  // the kernel just before) and the outputs are only touched after the predecessor is done
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (is_dq && ntiles > 0) load(0);
   // ---- stage Q (all threads): MT tiles x 128 rows x 16 chunks of 8 head dims; every load of
   // a thread is issued before its first store -----------------------------------------------
@@ -720,9 +726,17 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
       return QKV_ECUDA;
     attr_done |= 1u << (dev & 31);
   }
-  dim3 grid(p.tblocks, a.B * a.HKV, p.splits);
-  kern<<<grid, kThreadsTc, smem, st>>>(prm);
-  if (cudaGetLastError() != cudaSuccess) return QKV_ECUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.tblocks, a.B * a.HKV, p.splits);
+  cfg.blockDim = dim3(kThreadsTc, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, prm) != cudaSuccess) return QKV_ECUDA;
   if (direct || !combine) return QKV_OK;
   const long long rows = (long long)a.B * a.HQ * a.S;
   // the partials sit in the attention workspace: the combine clears what it reads

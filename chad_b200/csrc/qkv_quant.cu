@@ -23,18 +23,36 @@ __device__ __forceinline__ float load_as_f32<__nv_bfloat16>(const __nv_bfloat16*
 template <>
 __device__ __forceinline__ float load_as_f32<__half>(const __half* p) { return __half2float(*p); }
 
-// E = D/32 values per lane (2, 4 or 8); group of 64 = 64/E lanes.
+// One tensor to quantize-append: rows of x into (w, scales, biases).
+template <typename TIn, typename TS>
+struct QuantJob {
+  const TIn* x;
+  uint32_t* w;
+  TS* scales;
+  TS* biases;
+};
+
+// E = D/32 values per lane (2, 4 or 8); group of 64 = 64/E lanes. blockIdx.y picks the job
+// (K and V of one append share a launch).
 template <typename TIn, typename TS, int BITS, int D>
-__global__ void __launch_bounds__(128) quantize_rows_kernel(const TIn* __restrict__ x,
-                                                            uint32_t* __restrict__ w,
-                                                            TS* __restrict__ scales,
-                                                            TS* __restrict__ biases, int H, int S,
+__global__ void __launch_bounds__(128) quantize_rows_kernel(QuantJob<TIn, TS> j0,
+                                                            QuantJob<TIn, TS> j1, int H, int S,
                                                             int NP, int offset, long long n_rows) {
+  // Programmatic dependent launch: the attention kernel that follows may start streaming
+  // the older cache positions while this one runs; x is read only after the kernel that
+  // produced it is done.
+  asm volatile("griddepcontrol.launch_dependents;");
   constexpr int E = D / 32;
   constexpr int LPG = 64 / E;  // lanes per group
   constexpr int WPR = D * BITS / 32;
+  const QuantJob<TIn, TS>& job = blockIdx.y ? j1 : j0;
+  const TIn* __restrict__ x = job.x;
+  uint32_t* __restrict__ w = job.w;
+  TS* __restrict__ scales = job.scales;
+  TS* __restrict__ biases = job.biases;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (row >= n_rows) return;
   // row = ((b*H + h)*S + s); destination position offset + s of the (b,h) slab
   const long long bh = row / S;
@@ -131,50 +149,75 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ w, const TS* __re
 }
 
 template <typename TIn, typename TS, int BITS>
-static int launch_quantize_d(const void* x, void* w, void* sc, void* bi, int B, int H, int S,
-                             int D, int NP, int offset, cudaStream_t st) {
+static int launch_quantize_d(const void* const* x, void* const* w, void* const* sc,
+                             void* const* bi, int jobs, int B, int H, int S, int D, int NP,
+                             int offset, cudaStream_t st) {
   const long long rows = (long long)B * H * S;
   const int warps = 4;
-  const unsigned grid = (unsigned)((rows + warps - 1) / warps);
-#define QKV_Q_CASE(DD)                                                                   \
-  case DD:                                                                               \
-    quantize_rows_kernel<TIn, TS, BITS, DD><<<grid, warps * 32, 0, st>>>(                \
-        (const TIn*)x, (uint32_t*)w, (TS*)sc, (TS*)bi, H, S, NP, offset, rows);          \
-    break;
+  QuantJob<TIn, TS> j[2];
+  for (int i = 0; i < 2; ++i) {
+    const int k = i < jobs ? i : 0;
+    j[i] = QuantJob<TIn, TS>{(const TIn*)x[k], (uint32_t*)w[k], (TS*)sc[k], (TS*)bi[k]};
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((rows + warps - 1) / warps), (unsigned)jobs, 1);
+  cfg.blockDim = dim3(warps * 32, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaSuccess;
   switch (D) {
-    QKV_Q_CASE(64)
-    QKV_Q_CASE(128)
-    QKV_Q_CASE(256)
+    case 64:
+      e = cudaLaunchKernelEx(&cfg, quantize_rows_kernel<TIn, TS, BITS, 64>, j[0], j[1], H, S, NP, offset, rows);
+      break;
+    case 128:
+      e = cudaLaunchKernelEx(&cfg, quantize_rows_kernel<TIn, TS, BITS, 128>, j[0], j[1], H, S, NP, offset, rows);
+      break;
+    case 256:
+      e = cudaLaunchKernelEx(&cfg, quantize_rows_kernel<TIn, TS, BITS, 256>, j[0], j[1], H, S, NP, offset, rows);
+      break;
     default:
       return QKV_EUNSUPPORTED;
   }
-#undef QKV_Q_CASE
-  return QKV_OK;
+  return e == cudaSuccess ? QKV_OK : QKV_ECUDA;
 }
 
 template <typename TIn, typename TS>
-static int launch_quantize_b(const void* x, void* w, void* sc, void* bi, int B, int H, int S,
-                             int D, int NP, int offset, int bits, cudaStream_t st) {
-  if (bits == 4) return launch_quantize_d<TIn, TS, 4>(x, w, sc, bi, B, H, S, D, NP, offset, st);
-  return launch_quantize_d<TIn, TS, 8>(x, w, sc, bi, B, H, S, D, NP, offset, st);
+static int launch_quantize_b(const void* const* x, void* const* w, void* const* sc,
+                             void* const* bi, int jobs, int B, int H, int S, int D, int NP,
+                             int offset, int bits, cudaStream_t st) {
+  if (bits == 4)
+    return launch_quantize_d<TIn, TS, 4>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, st);
+  return launch_quantize_d<TIn, TS, 8>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, st);
+}
+
+int launch_quantize_jobs(const void* const* x, int x_dtype, void* const* w, void* const* sc,
+                         void* const* bi, int jobs, int B, int H, int S, int D, int NP,
+                         int offset, int bits, int scale_dtype, cudaStream_t st) {
+  if (B * (long long)H * S == 0) return QKV_OK;
+  if (jobs < 1 || jobs > 2) return QKV_EINVAL;
+  if (scale_dtype == QKV_BF16) {
+    if (x_dtype == QKV_BF16)
+      return launch_quantize_b<__nv_bfloat16, __nv_bfloat16>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
+    if (x_dtype == QKV_F16)
+      return launch_quantize_b<__half, __nv_bfloat16>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
+    return launch_quantize_b<float, __nv_bfloat16>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
+  }
+  if (x_dtype == QKV_BF16)
+    return launch_quantize_b<__nv_bfloat16, __half>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
+  if (x_dtype == QKV_F16)
+    return launch_quantize_b<__half, __half>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
+  return launch_quantize_b<float, __half>(x, w, sc, bi, jobs, B, H, S, D, NP, offset, bits, st);
 }
 
 int launch_quantize(const void* x, int x_dtype, void* w, void* sc, void* bi, int B, int H,
                     int S, int D, int NP, int offset, int bits, int scale_dtype,
                     cudaStream_t st) {
-  if (B * (long long)H * S == 0) return QKV_OK;
-  if (scale_dtype == QKV_BF16) {
-    if (x_dtype == QKV_BF16)
-      return launch_quantize_b<__nv_bfloat16, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
-    if (x_dtype == QKV_F16)
-      return launch_quantize_b<__half, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
-    return launch_quantize_b<float, __nv_bfloat16>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
-  }
-  if (x_dtype == QKV_BF16)
-    return launch_quantize_b<__nv_bfloat16, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
-  if (x_dtype == QKV_F16)
-    return launch_quantize_b<__half, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
-  return launch_quantize_b<float, __half>(x, w, sc, bi, B, H, S, D, NP, offset, bits, st);
+  return launch_quantize_jobs(&x, x_dtype, &w, &sc, &bi, 1, B, H, S, D, NP, offset, bits,
+                              scale_dtype, st);
 }
 
 int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, long long rows,

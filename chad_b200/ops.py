@@ -30,7 +30,14 @@ def dtype_code(t: Union[torch.Tensor, torch.dtype]) -> int:
     return _DT[dt]
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    # the raw handle of torch's current stream, without building a Stream object per call
+    if _RAW_STREAM is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _RAW_STREAM(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -123,9 +130,16 @@ _WS = {}
 
 
 def workspace_size(B: int, HQ: int, HKV: int, S: int, D: int, n_max: int, bits: int,
-                   group_size: int = GROUP_SIZE) -> int:
-    return _workspace_size(torch.cuda.current_device() if torch.cuda.is_available() else -1,
-                           B, HQ, HKV, S, D, n_max, bits, group_size)
+                   group_size: int = GROUP_SIZE, device: Optional[int] = None) -> int:
+    """Workspace bytes for calls with up to n_max keys. The need grows with n_max, so it is
+    asked for the next power of two: a decode loop, whose key count grows by one per step,
+    hits the memoized value instead of calling into the library every step."""
+    if device is None:
+        device = torch.cuda.current_device() if torch.cuda.is_available() else -1
+    n = 256
+    while n < n_max:
+        n *= 2
+    return _workspace_size(device, B, HQ, HKV, S, D, n, bits, group_size)
 
 
 @functools.lru_cache(maxsize=4096)
@@ -205,9 +219,10 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
         if t is not None and t.dtype != torch.int32:
             raise TypeError("lens/pos_base/total_lens must be int32")
     lib = _lib.load()
-    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size)
+    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size, dev.index)
     if splits:
-        need = max(need, splits * B * HQ * S * (D + 4) * 4 + (1 << 16))
+        # forced split count: rows of at most D + 16 floats per split (D + 2*D/32 merged)
+        need = max(need, splits * B * HQ * S * (D + 16) * 4 + (1 << 16))
     ws = workspace if workspace is not None else _workspace(dev, need)
     with _on(dev):
         check(lib.qkv_attention(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
@@ -230,9 +245,10 @@ def partials(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequence
     dev = _need_cuda(q, kw, ks, kb, vw, vs, vb, lens, pos_base, total_lens)
     B, HQ, S, D = q.shape
     HKV, NP = kw.shape[1], kw.shape[2]
-    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size)
+    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size, dev.index)
     if splits:
-        need = max(need, splits * B * HQ * S * (D + 4) * 4 + (1 << 16))
+        # forced split count: rows of at most D + 16 floats per split (D + 2*D/32 merged)
+        need = max(need, splits * B * HQ * S * (D + 16) * 4 + (1 << 16))
     if parts is None:
         parts = torch.empty(need // 4, dtype=torch.float32, device=q.device)
     kind, m, mnk, sb, sh, sq = _mask_args(mask, q, n)
@@ -279,7 +295,7 @@ def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     HKV, NP = kw.shape[1], kw.shape[2]
     if out is None:
         out = torch.empty_like(q)
-    need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size)
+    need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size, dev.index)
     ws = _workspace(dev, need)
     with _on(dev):
         check(_lib.load().qkv_prefill(
