@@ -7,7 +7,8 @@
 
 A step is one decode token through `--layers` (48) attention layers, each with its own
 quantized KV cache (inputs far larger than L2). The default workload is the 8-bit 32K
-decode (B1, HQ32, HKV4, D128, group 64): per layer one split-KV kernel + one combine.
+decode (B1, HQ32, HKV4, D128, group 64): per layer one split-KV kernel, whose last
+splits merge the partials.
 With N GPUs (torchrun, one process per GPU, NCCL) the sequence is sharded: every rank
 holds its own 32K-key shard of each layer (weak scaling, total context 32K*N), writes one
 (max, sum, out) partial per query row per layer, the partials of all layers meet in one
@@ -143,7 +144,8 @@ def run_chunk(args, cfg, rank, world, device):
         ms = float(t.item())
 
     # dominant kernel alone: prefill = the tensor-core kernel (one launch per layer when a
-    # single split covers the keys); verify = the split kernel without its combine
+    # single split covers the keys); verify = the same kernel's key-split partials without
+    # the combine that merges them
     if prefill:
         kern_us = ms * 1e3 / L
         kern_name = "prefill_tc_kernel"
@@ -170,7 +172,7 @@ def run_chunk(args, cfg, rank, world, device):
         e1.record()
         torch.cuda.synchronize()
         kern_us = e0.elapsed_time(e1) * 1e3 / (reps * L)
-        kern_name = "decode_split_kernel"
+        kern_name = "prefill_tc_kernel"
 
     # e2e: pinned host queries and new-token K/V in, quantize-append, attention, output out
     hq = torch.empty((L, B, HQ, S, D), dtype=torch.bfloat16).pin_memory()
@@ -580,7 +582,7 @@ def run_ours(args, cfg, rank, world, device):
             "parallelism": f"sequence-sharded split-KV x{world}" if world > 1 else "single GPU",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "decode_split_kernel",
+            "bound": "hbm", "kernel": "decode_kernel",
             "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
             "unit": "GB/s", "frac": round(achieved / peak, 4),
             "launch_us": round(split_us, 3), "bytes_per_launch": per_launch_bytes,
