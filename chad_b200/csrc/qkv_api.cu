@@ -347,19 +347,34 @@ int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, v
   if (rc) return rc;
   rc = check_append(v_new, dtype, vw, vs, vb, B, HKV, S, D, NP, offset, bits, group_size, dtype);
   if (rc) return rc;
-  // K and V of the new tokens in one launch
-  const void* xs[2] = {k_new, v_new};
-  void* ws_[2] = {kw, vw};
-  void* ss[2] = {ks, vs};
-  void* bs[2] = {kb, vb};
-  rc = launch_quantize_jobs(xs, dtype, ws_, ss, bs, 2, B, HKV, S, D, NP, offset, bits, dtype,
-                            static_cast<cudaStream_t>(stream));
-  if (rc) return fail(rc, "quantize: unsupported shape");
-  rc = cuda_check("qkv_prefill append");
+  AttnArgs a;
+  rc = setup_attn(a, q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, offset + S, nullptr,
+                  nullptr, nullptr, bits, group_size, dtype, scale, QKV_MASK_CAUSAL, nullptr, 0,
+                  0, 0, 0, 0, workspace, ws_bytes, true, true);
   if (rc) return rc;
-  return qkv_attention(q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, offset + S, nullptr,
-                       nullptr, nullptr, bits, group_size, dtype, scale, QKV_MASK_CAUSAL, nullptr,
-                       0, 0, 0, 0, QKV_OUT_NORMALIZED, 0, workspace, ws_bytes, stream);
+  a.out_kind = QKV_OUT_NORMALIZED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int R = (HQ / HKV) * S;
+  if (!a.use_tc && R <= decode_rows_per_group(R, D)) {
+    // one query-row group per kv head (a decode step, or a short draft block at small GQA):
+    // the attention kernel quantizes the new tokens into the cache itself, one launch
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.new_pos = offset;
+    rc = launch_decode(a, st);
+  } else {
+    // K and V of the new tokens in one launch, then attention
+    const void* xs[2] = {k_new, v_new};
+    void* ws_[2] = {kw, vw};
+    void* ss[2] = {ks, vs};
+    void* bs[2] = {kb, vb};
+    rc = launch_quantize_jobs(xs, dtype, ws_, ss, bs, 2, B, HKV, S, D, NP, offset, bits, dtype,
+                              st);
+    if (rc) return fail(rc, "quantize: unsupported shape");
+    rc = a.use_tc ? launch_prefill_tc(a, a.tc, true, st) : launch_decode(a, st);
+  }
+  if (rc) return fail(rc, "prefill: unsupported configuration");
+  return cuda_check("qkv_prefill");
 }
 
 }  // extern "C"

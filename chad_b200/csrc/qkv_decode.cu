@@ -37,6 +37,7 @@
 
 #include "qkv_common.cuh"
 #include "qkv_internal.h"
+#include "quant_row.cuh"
 
 namespace qkv {
 
@@ -320,6 +321,26 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
 
   if (warp == kWarps) {
     // ------------------------------ producer -------------------------------------------
+    if (a.k_new) {
+      // Fused append (one query-row group per kv head, so one CTA per key range): this CTA
+      // quantizes the new tokens that fall in its key range into the cache, with the same
+      // arithmetic as qkv_quantize_append, before its TMA reads them. The stages issued
+      // before the dependency wait stop short of these positions.
+      const int lo = max(a.new_pos, p_begin), hi = min(a.new_pos + a.S, p_end);
+      for (int pos = lo; pos < hi; ++pos) {
+        const long long src = (bh * a.S + (pos - a.new_pos)) * D;
+        const long long dst = bh * a.NP + pos;
+        quantize_row_warp<T, T, BITS, D>(
+            (const T*)a.k_new + src, (uint32_t*)a.kw + dst * (D * BITS / 32),
+            (T*)a.ks + dst * (D / 64), (T*)a.kb + dst * (D / 64), lane);
+        quantize_row_warp<T, T, BITS, D>(
+            (const T*)a.v_new + src, (uint32_t*)a.vw + dst * (D * BITS / 32),
+            (T*)a.vs + dst * (D / 64), (T*)a.vb + dst * (D / 64), lane);
+      }
+      // the rows written through the generic proxy are read below by TMA (async proxy)
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
+    }
     if (lane == 0) {
       bool ok = true;
       for (int it = pre; it < n_iters && ok; ++it) {

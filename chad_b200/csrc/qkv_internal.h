@@ -51,6 +51,9 @@ struct AttnArgs {
   int* status;  // device status word for bounded-wait failures
   int prefetch_limit;  // cache positions below this may be read before the kernel that
                        // precedes this one in the stream has finished (see qkv_decode.cu)
+  const void* k_new;   // decode path only: the S new tokens' K and V (B, HKV, S, D) in dtype,
+  const void* v_new;   // quantized into the cache at [new_pos, new_pos + S) by the attention
+  int new_pos;         // kernel itself before it reads them (nullptr: already in the cache)
   bool use_tc;         // multi-token tensor-core path (qkv_prefill_tc.cu) instead of decode
   TcPlan tc;
 };

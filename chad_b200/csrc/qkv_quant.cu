@@ -9,19 +9,9 @@
 // reference's attention (tests/test_mlx_qsdpa.py:45-49).
 #include "qkv_common.cuh"
 #include "qkv_internal.h"
+#include "quant_row.cuh"
 
 namespace qkv {
-
-template <typename TIn>
-__device__ __forceinline__ float load_as_f32(const TIn* p);
-template <>
-__device__ __forceinline__ float load_as_f32<float>(const float* p) { return *p; }
-template <>
-__device__ __forceinline__ float load_as_f32<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat162float(*p);
-}
-template <>
-__device__ __forceinline__ float load_as_f32<__half>(const __half* p) { return __half2float(*p); }
 
 // One tensor to quantize-append: rows of x into (w, scales, biases).
 template <typename TIn, typename TS>
@@ -42,8 +32,6 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(QuantJob<TIn, TS> j0
   // the older cache positions while this one runs; x is read only after the kernel that
   // produced it is done.
   asm volatile("griddepcontrol.launch_dependents;");
-  constexpr int E = D / 32;
-  constexpr int LPG = 64 / E;  // lanes per group
   constexpr int WPR = D * BITS / 32;
   const QuantJob<TIn, TS>& job = blockIdx.y ? j1 : j0;
   const TIn* __restrict__ x = job.x;
@@ -59,62 +47,8 @@ __global__ void __launch_bounds__(128) quantize_rows_kernel(QuantJob<TIn, TS> j0
   const int s = (int)(row - bh * S);
   const long long drow = bh * NP + offset + s;
 
-  float v[E];
-  const TIn* src = x + row * D + lane * E;
-#pragma unroll
-  for (int e = 0; e < E; ++e) v[e] = load_as_f32<TIn>(src + e);
-
-  float mx = v[0], mn = v[0];
-#pragma unroll
-  for (int e = 1; e < E; ++e) {
-    mx = fmaxf(mx, v[e]);
-    mn = fminf(mn, v[e]);
-  }
-#pragma unroll
-  for (int o = 1; o < LPG; o <<= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-  }
-  const float n_bins = float((1 << BITS) - 1);
-  float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), n_bins), 1e-7f);
-  const bool side = fabsf(mn) > fabsf(mx);
-  scale = side ? scale : -scale;
-  const float edge = side ? mn : mx;
-  const float q0 = rintf(__fdiv_rn(edge, scale));
-  float bias = 0.0f;
-  if (q0 != 0.0f) {
-    scale = __fdiv_rn(edge, q0);
-    bias = edge;
-  }
-
-  // pack this lane's E codes at bit offset (lane*E*BITS) % 32 of word (lane*E*BITS)/32
-  uint32_t part[(E * BITS + 31) / 32];
-#pragma unroll
-  for (int i = 0; i < (E * BITS + 31) / 32; ++i) part[i] = 0;
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    float c = rintf(__fdiv_rn(__fsub_rn(v[e], bias), scale));
-    c = fminf(fmaxf(c, 0.0f), n_bins);
-    const int bit = e * BITS;
-    part[bit / 32] |= uint32_t(c) << (bit % 32);
-  }
-  uint32_t* wrow = w + drow * WPR;
-  if constexpr (E * BITS >= 32) {
-#pragma unroll
-    for (int i = 0; i < E * BITS / 32; ++i) wrow[lane * (E * BITS / 32) + i] = part[i];
-  } else {
-    // several lanes share one word: OR their disjoint bit fields together
-    constexpr int LPW = 32 / (E * BITS);
-    uint32_t word = part[0] << ((lane % LPW) * E * BITS);
-#pragma unroll
-    for (int o = 1; o < LPW; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
-    if (lane % LPW == 0) wrow[lane / LPW] = word;
-  }
-  if (lane % LPG == 0) {
-    const int grp = lane / LPG;
-    scales[drow * (D / 64) + grp] = Elem<TS>::from_f32(scale);
-    biases[drow * (D / 64) + grp] = Elem<TS>::from_f32(bias);
-  }
+  quantize_row_warp<TIn, TS, BITS, D>(x + row * D, w + drow * WPR, scales + drow * (D / 64),
+                                      biases + drow * (D / 64), lane);
 }
 
 // One thread per packed word: 32/BITS outputs.

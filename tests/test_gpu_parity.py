@@ -269,3 +269,41 @@ def test_prefill_chunk_over_prefix():
     ref = orc.attention_quantized_fp32(q, kq, vq, D ** -0.5, prefix + S, 4, mask="causal")
     err = np.abs(f32_of(out) - ref)
     assert err.max() < 2e-2 and err.mean() < 2e-3
+
+
+@pytest.mark.parametrize("HQ,HKV,S,bits,n0", [
+    (32, 4, 1, 4, 4095),   # decode step, last position of the padded buffer
+    (32, 4, 1, 8, 777),
+    (16, 4, 2, 4, 1000),   # short draft block, one 8-row group per kv head
+    (32, 4, 2, 8, 2999),   # 16-row group
+    (8, 8, 4, 4, 3000),
+    (32, 2, 2, 4, 500),    # two row groups per kv head: the separate append launch
+])
+def test_prefill_decode_step_appends(HQ, HKV, S, bits, n0):
+    """qkv_prefill on the decode path: when one query-row group covers a kv head, the
+    attention kernel quantizes the new tokens into the cache itself (no append launch).
+    The rows it writes are bit-exact with the oracle's quantization, the older rows are
+    untouched, and the output over the whole cache matches the oracle."""
+    from chad_b200 import ops
+
+    n = n0 + S
+    D = 128
+    q, k, v = make_case(500 + n0 + S + bits, 1, HQ, HKV, S, D, n, "bf16", outliers=True)
+    c = _cache(k[:, :, :n0], v[:, :, :n0], bits, "bf16")
+    assert c.keys[0].shape[2] >= n
+    tq = torch_from_f32(q, "bf16")
+    kn = torch_from_f32(np.ascontiguousarray(k[:, :, n0:n]), "bf16")
+    vn = torch_from_f32(np.ascontiguousarray(v[:, :, n0:n]), "bf16")
+    out = ops.prefill(tq, kn, vn, c.keys, c.values, n0, bits, D ** -0.5)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for cache_t, x in ((c.keys, k), (c.values, v)):
+        w, s, b = _oracle_quant(x, bits, "bf16")
+        np.testing.assert_array_equal(u32_of(cache_t[0])[:, :, :n], w)
+        np.testing.assert_array_equal(bits_of(cache_t[1])[:, :, :n], s)
+        np.testing.assert_array_equal(bits_of(cache_t[2])[:, :, :n], b)
+    kq, vq = _oracle_quant(k, bits, "bf16"), _oracle_quant(v, bits, "bf16")
+    ref = orc.attention_quantized_fp32(q, kq, vq, D ** -0.5, n, bits, 64,
+                                       "causal" if S > 1 else None, "bf16")
+    err = np.abs(f32_of(out) - ref)
+    assert err.max() < 2e-2 and err.mean() < 2e-3
