@@ -157,6 +157,8 @@ int qkv_combine(const float* parts, int n_parts, long long rows, int D, void* ou
  * offset+S) (the cache quantizes before attention runs, src/chad/engine.py:941-990), then
  * attend the S queries over all offset+S keys, causal within the new chunk.
  * k_new / v_new: (B, HKV, S, D) in dtype. Other arguments as in qkv_attention.
+ * A decode step (one query-row group per kv head) is a single kernel launch: the attention
+ * kernel writes the new rows into the cache itself, bit-identical to qkv_quantize_append.
  */
 int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, void* ks,
                 void* kb, void* vw, void* vs, void* vb, void* out, int B, int HQ, int HKV,
