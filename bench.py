@@ -401,7 +401,7 @@ def run_ours(args, cfg, rank, world, device):
     part_local = torch.empty((L, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
     gathered = torch.empty((world, L, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
     ws_bytes = ops.workspace_size(B, HQ, HKV, 1, D, nloc, bits)
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)  # counters start at zero
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)  # the merge needs it zeroed
     keys_total = sum(loc)  # this rank's keys per layer (all batch rows)
     kv_bytes_rank = keys_total * HKV * kv_bytes_per_key(D, bits)
 
@@ -477,6 +477,39 @@ def run_ours(args, cfg, rank, world, device):
     e1.record()
     torch.cuda.synchronize()
     split_us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+
+    # ---- per-layer gather (N > 1): one all_gather + combine after every layer, as a model
+    # that serialises its layers must do; the timed step above gathers all layers at once
+    per_layer = None
+    if world > 1:
+        gl = torch.empty((world, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
+
+        def step_per_layer():
+            for l in range(L):
+                c = caches[l]
+                ops.attention(q[l], c.keys, c.values, scale, nloc, bits, lens=lens_t,
+                              out=part_local[l], out_kind=1, workspace=ws)
+                dist.all_gather_into_tensor(gl.view(-1), part_local[l].view(-1))
+                ops.combine(gl, torch.bfloat16)
+
+        for _ in range(2):
+            step_per_layer()
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps_pl = max(3, min(20, args.steps))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps_pl):
+            step_per_layer()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps_pl], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_pl = float(t.item())
+        per_layer = {"ms_per_step": round(ms_pl, 5), "us_per_layer": round(ms_pl * 1e3 / L, 3),
+                     "tok_per_s": round(B / (ms_pl * 1e-3), 1),
+                     "how": "one NCCL all_gather + combine after every layer, eager launches, "
+                            "max over ranks"}
 
     # ---- e2e through the public API with pinned host buffers ------------------------------
     hq = torch.empty((L, B, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
@@ -594,6 +627,8 @@ def run_ours(args, cfg, rank, world, device):
         "clocks": clocks.summary(),
         "gpu_launches": launches_per_step * args.steps,
     }
+    if per_layer is not None:
+        res["per_layer_gather"] = per_layer
     return res
 
 
