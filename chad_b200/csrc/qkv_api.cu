@@ -174,7 +174,10 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
                                                 decode_plan_balanced(B, HQ, HKV, S, D, bits)));
   // multi-token calls may take the tensor-core path: room for its split partials too
   if (prefill_tc_eligible(B, HQ, HKV, S, D, nullptr, nullptr, nullptr, QKV_MASK_CAUSAL)) {
-    const TcPlan tp = prefill_tc_plan(B, HQ, HKV, S, std::max(n_max, 1), 0);
+    // sized by the requested split count, so the answer never shrinks as n_max grows
+    // (callers may size once for an upper bound of the key count)
+    TcPlan tp = prefill_tc_plan(B, HQ, HKV, S, std::max(n_max, 1), 0);
+    tp.parts = tp.parts_bound;
     need = std::max(need, prefill_tc_workspace_bytes(B, HQ, S, D, tp, false));
   }
   return need;

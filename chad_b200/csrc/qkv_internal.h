@@ -16,6 +16,8 @@ struct TcPlan {
   int splits;           // CTAs along the keys
   int chunk;            // keys per split (multiple of the 128-key tile)
   int parts;            // partial rows per output row (splits, x2 when tiles == 1)
+  int parts_bound;      // parts at the requested split count, >= parts; unlike parts (whose
+                        // chunk rounding can lower it) it never decreases as n grows
 };
 
 // Everything one attention launch needs (device pointers; sizes already validated).

@@ -795,6 +795,7 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
   p.chunk = ((n + best - 1) / best + kKT - 1) / kKT * kKT;
   p.splits = (n + p.chunk - 1) / p.chunk;
   p.parts = p.splits * (p.tiles == 1 ? 2 : 1);
+  p.parts_bound = best * (p.tiles == 1 ? 2 : 1);
   return p;
 }
 

@@ -40,6 +40,23 @@ def test_version_and_workspace_size():
     assert lib.qkv_workspace_size(1, 30, 4, 1, 128, 32768, 4, 64) == 0  # HQ % HKV
 
 
+@pytest.mark.parametrize("B,HQ,HKV,S,D,bits", [
+    (1, 32, 4, 1, 128, 4), (1, 32, 4, 1, 128, 8), (4, 32, 4, 1, 128, 4), (1, 16, 2, 1, 256, 8),
+    (1, 32, 4, 8, 128, 4), (1, 32, 4, 2048, 128, 4), (2, 8, 8, 4, 64, 8), (3, 32, 2, 2, 128, 4),
+])
+def test_workspace_need_never_shrinks_as_keys_grow(B, HQ, HKV, S, D, bits):
+    """ops.workspace_size asks the library for the next power of two of the key count, which
+    is only safe if the need never shrinks as the key count grows."""
+    lib = _lib.load()
+    prev = 0
+    n = 1
+    while n <= 1 << 20:
+        need = lib.qkv_workspace_size(B, HQ, HKV, S, D, n, bits, 64)
+        assert need >= prev, (n, need, prev)
+        prev = need
+        n = n * 3 // 2 + 1
+
+
 def _attn(lib, **over):
     a = dict(q=16, kw=16, ks=16, kb=16, vw=16, vs=16, vb=16, out=16, B=1, HQ=16, HKV=2, S=1,
              D=128, NP=512, n=100, lens=None, pos_base=None, total_lens=None, bits=4, gs=64,
