@@ -38,19 +38,19 @@ if ROOT not in sys.path:
 import torch  # noqa: E402
 
 WORKLOADS = {
-    # the metric's 32K decode, 8-bit
+    # decode over 32K keys, 8-bit: B1, HQ32, HKV4, D128 (the headline workload)
     "decode32k-8bit": dict(B=1, HQ=32, HKV=4, D=128, N=32768, bits=8, ragged=False),
-    # the north-star target shape: same at 4-bit
+    # the same decode at 4-bit
     "decode32k-4bit": dict(B=1, HQ=32, HKV=4, D=128, N=32768, bits=4, ragged=False),
-    # B4, ragged 64K-128K, 4-bit, sequence split across the GPUs
+    # long context: B4, ragged 64K-128K keys, 4-bit, sequence split across the GPUs
     "longctx": dict(B=4, HQ=32, HKV=4, D=128, N=131072, bits=4, ragged=True),
 }
 # multi-token workloads (one GPU; with N GPUs every rank runs an independent replica)
 CHUNK_WORKLOADS = {
-    # 8 draft tokens at the tail of a 16K 4-bit cache, causal in the block
+    # speculative verify: 8 draft tokens at the tail of a 16K 4-bit cache, causal in the block
     "verify16k-4bit": dict(B=1, HQ=32, HKV=4, D=128, N=16384, S=8, bits=4, layers=48,
                            ragged=False),
-    # 2048 new tokens after a 30720-token 4-bit prefix, causal in the chunk
+    # prefill: 2048 new tokens after a 30720-token 4-bit prefix, causal in the chunk
     "prefill32k-4bit": dict(B=1, HQ=32, HKV=4, D=128, N=30720 + 2048, S=2048, bits=4, layers=8,
                             ragged=False),
 }

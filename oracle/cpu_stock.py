@@ -1,5 +1,5 @@
 """torch-CPU restatement of the reference's attention path over a quantized cache — TEST /
-BASELINE INFRASTRUCTURE ONLY (timed by bench.py's cpu_baseline and --impl reference legs;
+CPU BASELINE INFRASTRUCTURE ONLY (timed by bench.py's cpu_baseline and --impl reference legs;
 checked against qkv_oracle in tests; never imported by the product).
 
 It follows the stock route the reference takes where its fused kernel declines

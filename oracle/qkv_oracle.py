@@ -1,6 +1,6 @@
 """CPU oracle for the quantized-KV attention path — TEST INFRASTRUCTURE ONLY.
 
-This module is the checker, never the product: only `tests/`, `__graft_entry__.smoke()`
+This module is test infrastructure, never the product: only `tests/`, `__graft_entry__.smoke()`
 and the `cpu_baseline` / `--impl reference` legs of `bench.py` may import it. The
 product path (`chad_b200`) never calls into it and fails loudly when its CUDA library is
 missing.

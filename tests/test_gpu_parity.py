@@ -3,7 +3,8 @@
 Bit-exact for the integer/byte work (codes, scales, biases, dequantized K/V); within the
 reference's tolerance classes for attention output (tests/test_mlx_qsdpa.py:68-79:
 max-abs 2e-3 fp16 / 8e-3 bf16 against the dequantize->fp32 reference at head_dim 256,
-8-bit) and BASELINE's max-abs 2e-2 / mean-abs 2e-3 at the head_dim-128 configurations.
+8-bit) and max-abs 2e-2 / mean-abs 2e-3 at the head_dim-128 decode, verify and prefill
+shapes.
 """
 
 import numpy as np
@@ -48,7 +49,7 @@ def test_quantize_append_bit_exact(bits, D, dtype):
 
 
 def test_quantize_fp32_input_bf16_scales():
-    """K,V are fp32 N(0,1) with outliers, scales/biases stored in bf16."""
+    """Single-layer 4K decode inputs: K,V fp32 N(0,1) with key outliers, scales/biases in bf16."""
     from chad_b200 import ops
 
     rng = np.random.default_rng(5)

@@ -28,7 +28,7 @@ def test_pick_blocks_table():
 def test_covers_b200_surface():
     assert qsdpa.covers(256, 8)      # the reference's 35B shape
     assert qsdpa.covers(256, 4)      # its 9B shape
-    assert qsdpa.covers(128, 8)      # BASELINE shapes: covered here (not in the reference)
+    assert qsdpa.covers(128, 8)      # head_dim 128: covered here (not in the reference)
     assert qsdpa.covers(64, 2)
     assert not qsdpa.covers(96, 8)
     assert not qsdpa.covers(128, 8, bits=3)
@@ -61,7 +61,7 @@ def test_kv_bits_auto_defaults_on_for_covered_shapes():
     r = engine.resolve_kv_bits
     assert r(None, 256, 16, 2, True) == 8     # 35B: gqa 8
     assert r(None, 256, 16, 4, True) == 8     # 9B: gqa 4
-    assert r(None, 128, 32, 4, True) == 8     # BASELINE shape: covered on B200
+    assert r(None, 128, 32, 4, True) == 8     # head_dim 128, GQA 8: covered on B200
     assert r(None, 96, 16, 2, True) is None   # head_dim not covered
     assert r(None, 256, 16, 0, True) is None  # shape unknown
     assert r(None, 256, 16, 2, False) is None  # kernel absent
