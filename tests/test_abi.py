@@ -108,3 +108,18 @@ def test_check_raises_with_message():
     with pytest.raises(_lib.QKVError) as e:
         _lib.check(rc)
     assert "head_dim" in str(e.value)
+
+
+@pytest.mark.parametrize("B,HQ,HKV,S,D,bits", [
+    (1, 32, 4, 1, 128, 8), (1, 32, 4, 8, 128, 4), (1, 32, 4, 16, 128, 8), (4, 32, 4, 1, 128, 4),
+    (1, 32, 4, 2048, 128, 4), (2, 64, 8, 8, 128, 4),
+])
+def test_python_workspace_estimate_covers_every_key_count(B, HQ, HKV, S, D, bits):
+    """ops.workspace_size memoizes by power-of-two key count: its answer must cover the
+    library's exact need at every key count below that power of two."""
+    from chad_b200 import ops
+
+    lib = _lib.load()
+    for n in list(range(1, 40000, 97)) + [8191, 8192, 8193, 8696, 16384, 16385, 131072]:
+        assert ops.workspace_size(B, HQ, HKV, S, D, n, bits) >= \
+            lib.qkv_workspace_size(B, HQ, HKV, S, D, n, bits, 64), n
