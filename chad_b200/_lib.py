@@ -31,7 +31,10 @@ SIGNATURES = {
     "qkv_version": (_i, []),
     "qkv_last_error": (ctypes.c_char_p, []),
     "qkv_device_status": (_i, [_vp, _i]),
+    "qkv_test_hooks": (_i, [_i, _ll]),
     "qkv_quantize_append": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "qkv_quantize_append_kv": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "qkv_dequantize": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
     "qkv_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i, _i]),
     "qkv_attention": (

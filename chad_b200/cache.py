@@ -100,6 +100,14 @@ class QuantizedKVCache:
                 dst[:, :, : self.offset].copy_(src[:, :, : self.offset])
         self.keys, self.values = nk, nv
 
+    def reserve(self, n: int, b: int, h: int, d: int, dtype: torch.dtype,
+                device: torch.device) -> None:
+        """Pre-size the buffers for n positions (rounded up to whole steps) so that appends
+        up to n never grow them. mlx-lm grows by one step per crossing, copying the valid
+        prefix each time; a decode loop that knows its budget avoids those copies."""
+        if n > self.capacity:
+            self._grow(n, b, h, d, d, dtype, device)
+
     @property
     def capacity(self) -> int:
         return 0 if self.keys is None else self.keys[0].shape[2]
@@ -114,8 +122,12 @@ class QuantizedKVCache:
         prev = self.offset
         if self.keys is None or prev + s > self.capacity:
             self._grow(prev + s, b, h, dk, dv, keys.dtype, keys.device)
-        ops.quantize_append(keys.contiguous(), *self.keys, prev, self.bits, self.group_size)
-        ops.quantize_append(values.contiguous(), *self.values, prev, self.bits, self.group_size)
+        k, v = keys.contiguous(), values.contiguous()
+        if k.shape == v.shape and k.dtype == v.dtype:
+            ops.quantize_append_kv(k, v, self.keys, self.values, prev, self.bits, self.group_size)
+        else:  # (different K and V head dims)
+            ops.quantize_append(k, *self.keys, prev, self.bits, self.group_size)
+            ops.quantize_append(v, *self.values, prev, self.bits, self.group_size)
         self.offset = prev + s
         return self.fetch()
 

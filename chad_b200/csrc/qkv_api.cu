@@ -6,6 +6,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "../../include/qkv.h"
 #include "qkv_internal.h"
@@ -16,8 +17,16 @@ namespace qkv {
 __device__ int g_device_status = 0;
 
 namespace {
+std::atomic<int> g_hook_phantom{0};
+std::atomic<long long> g_hook_spin_ns{0};
+}  // namespace
+
+TestHooks test_hooks() { return TestHooks{g_hook_phantom.load(), g_hook_spin_ns.load()}; }
+
+namespace {
 
 thread_local char g_err[512] = "";
+thread_local size_t g_last_need = 0;
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -37,9 +46,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int* status_ptr() {
   // Address of the device status word on the current device, looked up once per device.
-  static int* ptrs[64] = {nullptr};
+  static int* ptrs[kMaxDevices] = {nullptr};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   if (!ptrs[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
@@ -63,10 +72,10 @@ int check_cache_shape(int D, int bits, int group_size) {
 }  // namespace
 
 int num_sms() {
-  static int cached[64] = {0};
+  static int cached[kMaxDevices] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
   if (!cached[dev]) {
     int v = 0;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
@@ -75,6 +84,8 @@ int num_sms() {
   }
   return cached[dev];
 }
+
+size_t last_workspace_need() { return g_last_need; }
 
 int set_last_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -103,12 +114,25 @@ int qkv_device_status(void* stream, int reset) {
       cudaStreamSynchronize(st) != cudaSuccess)
     return cuda_check("qkv_device_status");
   if (reset) {
+    // The stream is synchronized: every kernel enqueued before this call has finished, so
+    // no partial row can still land in the static scratch of qkv_attention_noalloc, which
+    // is zeroed here (the merge reads a zero word as "not yet written"; a merge that gave up
+    // may have left words behind).
     const int zero = 0;
     if (cudaMemcpyAsync(p, &zero, sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
+        noalloc_scratch_clear(st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
       return cuda_check("qkv_device_status reset");
   }
   return v;
+}
+
+int qkv_test_hooks(int phantom_splits, long long spin_ns) {
+  if (phantom_splits < 0 || phantom_splits > 64 || spin_ns < 0)
+    return fail(QKV_EINVAL, "bad test hook values (phantom %d, spin %lld ns)", phantom_splits,
+                spin_ns);
+  g_hook_phantom.store(phantom_splits);
+  g_hook_spin_ns.store(spin_ns);
+  return QKV_OK;
 }
 
 namespace {
@@ -142,6 +166,26 @@ int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void*
   return cuda_check("qkv_quantize_append");
 }
 
+int qkv_quantize_append_kv(const void* k, const void* v, int x_dtype, void* kw, void* ks,
+                           void* kb, void* vw, void* vs, void* vb, int B, int H, int S, int D,
+                           int NP, int offset, int bits, int group_size, int scale_dtype,
+                           void* stream) {
+  int rc = check_append(k, x_dtype, kw, ks, kb, B, H, S, D, NP, offset, bits, group_size,
+                        scale_dtype);
+  if (rc) return rc;
+  rc = check_append(v, x_dtype, vw, vs, vb, B, H, S, D, NP, offset, bits, group_size,
+                    scale_dtype);
+  if (rc) return rc;
+  const void* xs[2] = {k, v};
+  void* ws_[2] = {kw, vw};
+  void* ss[2] = {ks, vs};
+  void* bs[2] = {kb, vb};
+  rc = launch_quantize_jobs(xs, x_dtype, ws_, ss, bs, 2, B, H, S, D, NP, offset, bits,
+                            scale_dtype, static_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "quantize: unsupported shape");
+  return cuda_check("qkv_quantize_append_kv");
+}
+
 int qkv_dequantize(const void* w, const void* scales, const void* biases, void* out,
                    long long rows, int D, int bits, int group_size, int dtype, int round_mode,
                    void* stream) {
@@ -162,12 +206,9 @@ size_t qkv_workspace_size(int B, int HQ, int HKV, int S, int D, int n_max, int b
   (void)bits;
   (void)group_size;
   if (B <= 0 || HQ <= 0 || HKV <= 0 || S <= 0 || D <= 0 || HQ % HKV) return 0;
-  const int R = (HQ / HKV) * S;
-  const int rg = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
-  (void)rg;
-  int splits = 1, chunk = 16, cluster = 1;
-  decode_plan(B, HQ, HKV, S, D, bits, std::max(n_max, 1), 0, &splits, &chunk, &cluster);
-  size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, splits, cluster);
+  int splits = 1, chunk = 16;
+  decode_plan(B, HQ, HKV, S, D, bits, std::max(n_max, 1), 0, &splits, &chunk);
+  size_t need = decode_workspace_bytes(B, HQ, S, D, splits);
   // ragged batches (per-batch lengths) share the CTAs by key count
   if (B > 1)
     need = std::max(need, decode_balanced_bytes(B, HQ, S, D,
@@ -256,8 +297,8 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
   if ((long long)HKV * rg > 65535 || B > 65535)
     return fail(QKV_EUNSUPPORTED, "too many kv heads x query-row groups (%lld) or batch (%d)",
                 (long long)HKV * rg, B);
-  decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk, &a.cluster);
-  size_t need = decode_workspace_bytes(B, HQ, HKV, S, D, a.splits, a.cluster);
+  decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &a.splits, &a.chunk);
+  size_t need = decode_workspace_bytes(B, HQ, S, D, a.splits);
   if (merge && lens && B > 1 && splits == 0) {
     // ragged batches: share the CTAs by key count instead of splitting every batch alike
     a.balanced = decode_plan_balanced(B, HQ, HKV, S, D, bits);
@@ -271,6 +312,15 @@ int setup_attn(AttnArgs& a, const void* q, const void* kw, const void* ks, const
     a.tc = prefill_tc_plan(B, HQ, HKV, S, n_max, splits);
     need = prefill_tc_workspace_bytes(B, HQ, S, D, a.tc, direct);
   }
+  if (merge && !a.use_tc) {
+    const TestHooks h = test_hooks();
+    if (!a.balanced && h.phantom_splits > 0) {
+      a.phantom = h.phantom_splits;
+      need = decode_workspace_bytes(B, HQ, S, D, a.splits + a.phantom);
+    }
+    a.spin_ns = (unsigned long long)h.spin_ns;
+  }
+  g_last_need = need;
   if (!workspace || ws_bytes < need)
     return fail(QKV_EWORKSPACE, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (!aligned16(workspace)) return fail(QKV_EALIGN, "workspace must be 16-byte aligned");
@@ -318,7 +368,7 @@ int qkv_partials(const void* q, const void* kw, const void* ks, const void* kb, 
                       false);
   if (rc) return rc;
   a.out_kind = QKV_OUT_PARTIAL;
-  *n_parts = a.use_tc ? a.tc.parts : a.splits / a.cluster;
+  *n_parts = a.use_tc ? a.tc.parts : a.splits;
   rc = a.use_tc ? launch_prefill_tc(a, a.tc, false, static_cast<cudaStream_t>(stream))
                 : launch_split_only(a, static_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "partials: unsupported configuration");

@@ -4,21 +4,22 @@
 // simdgroup-matrix retile `_P1_SGM_SRC`, :303-473) and pass 2 (`_P2_SRC`, :213-265).
 //
 // Work split. One CTA = one (batch b, kv head, query-row group, key split); its query rows
-// are the GQA heads x query tokens that share the kv head (at most 16, contiguous in q).
-// Consecutive splits of the same rows form a thread-block cluster (up to 8 CTAs).
+// are the GQA heads x query tokens that share the kv head (8 or 16, contiguous in q). With
+// per-batch lengths and an in-kernel merge, the CTAs of a (kv head, row group) are shared
+// by the batches in proportion to their key counts instead (balanced mode).
 //
-// Memory path. A producer warp streams 64-key stages into a shared-memory ring: K and V code
-// tiles with 2-D TMA tensor copies (swizzled so that every consumer read below is free of
-// bank conflicts) and the four scale/bias arrays with 1-D bulk copies, all completing on
-// mbarriers. No multicast.
+// Memory path. A producer warp streams stages of 64 or 128 keys into a shared-memory ring:
+// K and V code tiles with 3-D TMA tensor copies (swizzled so that every consumer read below
+// is free of bank conflicts) and the four scale/bias arrays with 1-D bulk copies, all
+// completing on mbarriers. No multicast.
 //
-// Math. Four consumer warps take 16 keys each per stage and run mma.sync m16n8k16 with the
-// 16 KEYS as the M rows and the query rows as the N columns (GQA 8 fills N=8 exactly). The
-// packed codes are fed to the tensor cores as they are: AND-ing a 4-bit code into the low
-// bits of an f16 (or placing an 8-bit code there with PRMT) gives the subnormal f16 value
-// code * 2^-24 exactly, and B200's f16 MMA is exact on subnormal inputs. Because every
-// k-step of QK (and every m-tile of PV) stays inside one 64-wide scale group, the affine
-// parameters factor out of the products:
+// Math. Four consumer warps take 16 (or 2 x 16) keys each per stage and run mma.sync
+// m16n8k16 with the 16 KEYS as the M rows and the query rows as the N columns (GQA 8 fills
+// N=8 exactly). The packed codes are fed to the tensor cores as they are: AND-ing a 4-bit
+// code into the low bits of an f16 (or placing an 8-bit code there with PRMT) gives the
+// subnormal f16 value code * 2^-24 exactly, and B200's f16 MMA is exact on subnormal
+// inputs. Because every k-step of QK (and every m-tile of PV) stays inside one 64-wide
+// scale group, the affine parameters factor out of the products:
 //   score(key, row)  = sum_g s[key,g] * 2^24 * (codes_g . q_g)  +  sum_g b[key,g] * sum(q_g)
 //   out(dim g, row) += 2^24 * sum_key (p * s[key,g]) * code  +  sum_key p * b[key,g]
 // so no per-element dequantisation arithmetic is left: per code the kernel spends one
@@ -26,9 +27,12 @@
 // the score accumulator with movmatrix.trans (no shared-memory round trip).
 //
 // Reduction. Online softmax in base 2; the four warps merge through shared memory into one
-// CTA partial (out, max, sum); the CTAs of a cluster merge those through distributed shared
-// memory into one cluster partial in global memory; a combine kernel (the reference's pass
-// 2), chained by programmatic dependent launch, merges the cluster partials.
+// CTA partial (out, max, sum), which the CTA stores to the workspace as self-validating
+// words (see store_part). The last splits of each row group then merge every split's
+// partial inside the same kernel, one (row, 32-dim slice) unit per merging CTA, and write
+// the output: the reference's pass 2 without a second launch. qkv_partials stops after the
+// stores (plain floats) and leaves the merge to combine_kernel, which also serves the
+// cross-GPU merge and grids too large to be resident in one wave.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -180,6 +184,9 @@ struct DecodeParams {
   CUtensorMap tmv;  // V codes
   float* gpart;     // per-CTA partial rows [splits][B*HQ*S][D+4], or [..][D+2*D/32] encoded
   int merge;        // 1: the row group's last splits merge the partials into a.out
+  int phantom;      // test hook: partial sets the mergers wait for that no CTA writes
+  unsigned long long spin_ns;  // bound on the merge's polling (kSpinNanos unless a test
+                               // hook shortens it)
 };
 
 template <typename T, int BITS, int D, int NT>
@@ -817,6 +824,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
   const int nm = min(nsplit, units);
   const int first = nsplit - nm;
   if (split < first) return;
+  const int nwait = nsplit + P.phantom;  // partial sets to merge (phantom: a test hook)
   // the merge scratch reuses the stage ring: no thread (the producer warp's lanes included,
   // which may have nothing to poll) writes it before every consumer is done with the ring
   __syncthreads();
@@ -833,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
       // this thread's partials: p = slot, slot + kMergeSlots, ... in batches of 8 (online).
       // Every thread runs every batch (a slot past the last split just has nothing to
       // load), so the warp votes in the poll below always see all 32 lanes.
-      for (int b0 = 0; b0 < nsplit; b0 += 8 * kMergeSlots) {
+      for (int b0 = 0; b0 < nwait; b0 += 8 * kMergeSlots) {
         const int p0 = b0 + slot;
         float pm[8], pl[8];
         float4 po[8];
@@ -843,7 +851,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
           pm[k] = kNegInf;
           pl[k] = 0.f;
           po[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (p0 + k * kMergeSlots < nsplit) need |= 1u << k;
+          if (p0 + k * kMergeSlots < nwait) need |= 1u << k;
         }
         const unsigned want = need;
         unsigned long long t0 = 0;
@@ -867,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
           if (!__any_sync(0xffffffffu, need)) break;
           const unsigned long long now = global_ns();
           if (t0 == 0) t0 = now;
-          if (__any_sync(0xffffffffu, now - t0 > kSpinNanos)) {  // (one verdict per warp)
+          if (__any_sync(0xffffffffu, now - t0 > P.spin_ns)) {  // (one verdict per warp)
             flag_device_error(a.status, 14);
             break;
           }
@@ -1094,6 +1102,8 @@ int launch_split(const AttnArgs& a, bool merge, cudaStream_t st) {
   p.a = a;
   p.merge = merge ? 1 : 0;
   p.gpart = reinterpret_cast<float*>(a.workspace);
+  p.phantom = merge ? a.phantom : 0;
+  p.spin_ns = a.spin_ns ? a.spin_ns : kSpinNanos;
   if (!make_code_map<BITS, D>(&p.tmk, a.kw, a.NP, (long long)a.B * a.HKV) ||
       !make_code_map<BITS, D>(&p.tmv, a.vw, a.NP, (long long)a.B * a.HKV))
     return QKV_ECUDA;
@@ -1199,7 +1209,7 @@ int round_chunk(int n_max, int sp) {
 // Split plan: as many co-resident CTAs as the GPU holds in one wave (the in-kernel merge's
 // last arrivals wait for the rest of their row group), at least 16 keys per split.
 void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want,
-                 int* splits, int* chunk, int* cluster) {
+                 int* splits, int* chunk) {
   const int R = (HQ / HKV) * S;
   const int rgs = (R + decode_rows_per_group(R, D) - 1) / decode_rows_per_group(R, D);
   const int units = std::max(1, B * HKV * rgs);
@@ -1214,13 +1224,7 @@ void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int 
   }
   sp = std::min(std::min(sp, max_sp), kMaxSplits);
   *splits = sp;
-  *cluster = 1;
   *chunk = round_chunk(n_max, sp);
-}
-
-size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster) {
-  (void)cluster;
-  return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
 }
 
 int decode_plan_balanced(int B, int HQ, int HKV, int S, int D, int bits) {
@@ -1237,16 +1241,40 @@ size_t decode_balanced_bytes(int B, int HQ, int S, int D, int balanced) {
   return (size_t)(balanced + B) * HQ * S * (D + 2 * (D / 32)) * sizeof(float);
 }
 
-size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster) {
-  (void)HKV;
-  (void)cluster;
+size_t decode_workspace_bytes(int B, int HQ, int S, int D, int splits) {
   // encoded partial rows: D values and one (max, sum) pair per 32-dim merge slice
   return (size_t)splits * B * HQ * S * (D + 2 * (D / 32)) * sizeof(float);
 }
 
 int launch_split_only(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, false, st); }
 
-int launch_decode(const AttnArgs& a, cudaStream_t st) { return launch_split_any(a, true, st); }
+size_t decode_fallback_bytes(int B, int HQ, int S, int D, int splits) {
+  return (size_t)splits * B * HQ * S * (D + 4) * sizeof(float);
+}
+
+bool decode_merges_in_kernel(const AttnArgs& a) {
+  // The merging splits wait for the other CTAs of their row group, so every CTA of the
+  // grid must be able to hold an SM slot at once: the split plan keeps automatic grids to
+  // one wave, and balanced grids are one wave by construction. A forced split count past
+  // that takes the two-launch route instead (plain partial rows, then combine_kernel).
+  if (a.balanced) return true;
+  const int R = (a.HQ / a.HKV) * a.S;
+  const int rg = (R + decode_rows_per_group(R, a.D) - 1) / decode_rows_per_group(R, a.D);
+  const long long ctas = (long long)a.splits * a.HKV * rg * a.B;
+  int cap = max_ctas_any(a.bits, a.D, R);
+  if (cap <= 0) cap = decode_ctas_per_sm(R, a.D, a.bits) * num_sms();
+  return ctas <= cap;
+}
+
+int launch_decode(const AttnArgs& a, cudaStream_t st) {
+  if (decode_merges_in_kernel(a)) return launch_split_any(a, true, st);
+  int rc = launch_split_any(a, false, st);
+  if (rc) return rc;
+  const long long rows = (long long)a.B * a.HQ * a.S;
+  // combine clears every word it reads: the workspace is left zero for the next call
+  return launch_combine(reinterpret_cast<const float*>(a.workspace), a.splits, rows, rows, a.D,
+                        a.out, a.dtype, a.out_kind, st, true);
+}
 
 int launch_combine(const float* parts, int n_parts, long long part_stride_rows, long long rows,
                    int D, void* out, int out_dtype, int out_kind, cudaStream_t st, bool clear) {

@@ -43,9 +43,8 @@ struct AttnArgs {
   int mask_nk;
   long long mask_sb, mask_sh, mask_sq;
   int out_kind;
-  int splits;   // resolved split count (>= 1, a multiple of cluster)
+  int splits;   // resolved split count (>= 1)
   int chunk;    // keys per split (multiple of the 16-key warp tile)
-  int cluster;  // CTAs per thread-block cluster along the splits (1..8)
   int balanced; // > 0 (ragged lens, merged in-kernel): the splits CTAs of a (kv head, row
                 // group) are shared by the batches by key count, chunk = total / balanced
   void* workspace;
@@ -58,16 +57,24 @@ struct AttnArgs {
   int new_pos;         // kernel itself before it reads them (nullptr: already in the cache)
   bool use_tc;         // multi-token tensor-core path (qkv_prefill_tc.cu) instead of decode
   TcPlan tc;
+  int phantom;                 // test hook (qkv_test_hooks): extra partial sets to wait for
+  unsigned long long spin_ns;  // test hook: merge polling bound (0 = the library default)
 };
+
+// Values set by qkv_test_hooks (0 = off / library default).
+struct TestHooks {
+  int phantom_splits;
+  long long spin_ns;
+};
+TestHooks test_hooks();
 
 // Split-KV decode/verify path (mma.sync, keys as MMA rows, query rows as columns).
 // The attention workspace holds partial rows whose words read 0 until written; it is zero
 // before the first call and every call leaves it zero (the readers clear what they read).
 int decode_rows_per_group(int R, int D);    // query rows handled by one CTA (8 or 16)
-size_t decode_workspace_bytes(int B, int HQ, int HKV, int S, int D, int splits, int cluster);
-size_t decode_partials_bytes(int B, int HQ, int S, int D, int splits, int cluster);
+size_t decode_workspace_bytes(int B, int HQ, int S, int D, int splits);
 void decode_plan(int B, int HQ, int HKV, int S, int D, int bits, int n_max, int want_splits,
-                 int* splits, int* chunk, int* cluster);
+                 int* splits, int* chunk);
 // Ragged batches merged in-kernel: CTAs per (kv head, row group) shared by the batches
 // (= balanced + B); returns balanced. The workspace need is decode_balanced_bytes.
 int decode_plan_balanced(int B, int HQ, int HKV, int S, int D, int bits);
@@ -77,7 +84,12 @@ inline int decode_ctas_per_sm(int R, int D, int bits) {
   return (R <= 8 && D <= 128 && bits == 8) ? 3 : 2;
 }
 
-int launch_decode(const AttnArgs& a, cudaStream_t st);  // split kernel + combine
+// Decode/verify attention: one launch whose last splits merge the partials, or (a grid too
+// large to be resident at once) the split kernel's plain partial rows + combine_kernel.
+int launch_decode(const AttnArgs& a, cudaStream_t st);
+bool decode_merges_in_kernel(const AttnArgs& a);
+// workspace of the two-launch route: plain partial rows [splits][B*HQ*S][D+4]
+size_t decode_fallback_bytes(int B, int HQ, int S, int D, int splits);
 int launch_split_only(const AttnArgs& a, cudaStream_t st);  // partial rows into a.workspace
 
 // clear: the partials are in an attention workspace; zero every word read
@@ -97,6 +109,13 @@ int launch_dequantize(const void* w, const void* sc, const void* bi, void* out, 
 
 int num_sms();
 
+// Per-device caches in this library are indexed by device ordinal below this bound.
+constexpr int kMaxDevices = 64;
+
+// Zero the static scratch of qkv_attention_noalloc on the current device (enqueued on st);
+// cudaSuccess without work when no call has resolved the scratch on this device yet.
+cudaError_t noalloc_scratch_clear(cudaStream_t st);
+
 // Byte-typed tiled tensor map over (RB, NP, bhs) packed codes; box (box_inner bytes,
 // box_rows keys, 1), swizzled by the box's inner span. False if the driver refuses it.
 bool make_code_map_bytes(CUtensorMap* m, const void* base, int RB, int NP, long long bhs,
@@ -110,6 +129,10 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
 size_t prefill_tc_workspace_bytes(int B, int HQ, int S, int D, const TcPlan& p, bool direct);
 // combine = false leaves the split partials in a.workspace ([splits][B*HQ*S][D+4]).
 int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st);
+
+// Workspace bytes the last attention call on this thread asked for (set whenever its
+// arguments were valid enough to plan the launch).
+size_t last_workspace_need();
 
 // Record a message for qkv_last_error() on this thread and return `code`.
 int set_last_error(int code, const char* fmt, ...);

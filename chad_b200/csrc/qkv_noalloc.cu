@@ -18,7 +18,12 @@
 // partial-row word as "not yet written" while it is zero and zeroes every word it reads, so
 // the array starts at zero (static storage is zero-initialized) and every call returns it to
 // zero. Two calls whose kernels overlap on the GPU (for example on two streams at once) race
-// on the array: serialize them.
+// on the array: serialize them. A merge that gave up on a bounded wait (reported later by
+// qkv_device_status as QKV_EDEVICE) can leave words behind; qkv_device_status(stream, 1)
+// synchronizes the stream and zeroes the array again (a memset, not an allocation).
+//
+// The address looked up at set-up stays cached for the life of the process: after a
+// cudaDeviceReset, restart the process before calling this entry point again.
 #include <algorithm>
 
 #include "../../include/qkv.h"
@@ -32,29 +37,48 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+void* g_scratch_ptrs[kMaxDevices] = {nullptr};
+
 // Device address of g_noalloc_scratch on the current device (looked up once per device).
-void* noalloc_scratch(int* err) {
-  static void* ptrs[64] = {nullptr};
+// Returns a QKV status; *out receives the address.
+int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    *err = (int)e;
-    return nullptr;
-  }
-  if (!ptrs[dev]) {
+  if (e != cudaSuccess)
+    return set_last_error(QKV_ECUDA, "qkv_attention_noalloc: cudaGetDevice failed: %s",
+                          cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_last_error(QKV_EUNSUPPORTED,
+                          "qkv_attention_noalloc: device ordinal %d is beyond the %d devices "
+                          "this library tracks",
+                          dev, kMaxDevices);
+  if (!g_scratch_ptrs[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
-      *err = (int)e;
       cudaGetLastError();
-      return nullptr;
+      return set_last_error(QKV_ECUDA,
+                            "qkv_attention_noalloc: cannot resolve the static scratch on "
+                            "device %d: %s",
+                            dev, cudaGetErrorString(e));
     }
-    ptrs[dev] = p;
+    g_scratch_ptrs[dev] = p;
   }
-  return ptrs[dev];
+  *out = g_scratch_ptrs[dev];
+  return QKV_OK;
 }
 
 }  // namespace
+
+cudaError_t noalloc_scratch_clear(cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return cudaSuccess;  // nothing of ours can be on such a device
+  }
+  if (!g_scratch_ptrs[dev]) return cudaSuccess;  // never used here: still zero
+  return cudaMemsetAsync(g_scratch_ptrs[dev], 0, kNoAllocScratchBytes, st);
+}
 
 }  // namespace qkv
 
@@ -67,35 +91,20 @@ extern "C" int qkv_attention_noalloc(const void* q, const void* kw, const void* 
                                      long long mask_sb, long long mask_sh, long long mask_sq,
                                      int out_kind, int splits, void* stream) {
   using namespace qkv;
-  // Scratch the call needs, computed the way qkv_attention sizes its split; argument errors
-  // are left to qkv_attention's own validation.
-  if (B > 0 && HQ > 0 && HKV > 0 && S > 0 && HQ % HKV == 0 && n >= 0 && splits >= 0 &&
-      (D == 64 || D == 128 || D == 256)) {
-    const int n_max = std::max(lens ? std::min(n, std::max(NP, 0)) : n, 1);
-    size_t need;
-    if (splits == 0) {
-      need = qkv_workspace_size(B, HQ, HKV, S, D, n_max, bits, group_size);
-    } else {
-      int sp = 1, ch = 16, cl = 1;
-      decode_plan(B, HQ, HKV, S, D, bits, n_max, splits, &sp, &ch, &cl);
-      need = decode_workspace_bytes(B, HQ, HKV, S, D, sp, cl);
-    }
-    if (need > kNoAllocScratchBytes)
-      return set_last_error(QKV_EWORKSPACE,
-                            "qkv_attention_noalloc: this call needs %zu bytes of scratch, more "
-                            "than the %zu-byte static scratch; use qkv_attention with a "
-                            "caller-owned workspace",
-                            need, kNoAllocScratchBytes);
-  }
-  int err = 0;
-  void* ws = noalloc_scratch(&err);
-  if (!ws)
-    return set_last_error(QKV_ECUDA,
-                          "qkv_attention_noalloc: cannot resolve the static scratch on this "
-                          "device (cuda error %d)",
-                          err);
-  return qkv_attention(q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, n, lens, pos_base,
-                       total_lens, bits, group_size, dtype, scale, mask_kind, mask, mask_nk,
-                       mask_sb, mask_sh, mask_sq, out_kind, splits, ws, kNoAllocScratchBytes,
-                       stream);
+  void* ws = nullptr;
+  int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  // The plan (and so the scratch it needs) is the one qkv_attention makes for these
+  // arguments; a call that needs more than the static scratch is refused by its own check.
+  rc = qkv_attention(q, kw, ks, kb, vw, vs, vb, out, B, HQ, HKV, S, D, NP, n, lens, pos_base,
+                     total_lens, bits, group_size, dtype, scale, mask_kind, mask, mask_nk,
+                     mask_sb, mask_sh, mask_sq, out_kind, splits, ws, kNoAllocScratchBytes,
+                     stream);
+  if (rc == QKV_EWORKSPACE)
+    return set_last_error(QKV_EWORKSPACE,
+                          "qkv_attention_noalloc: this call needs %zu bytes of scratch, more "
+                          "than the %zu-byte static scratch; use qkv_attention with a "
+                          "caller-owned workspace",
+                          last_workspace_need(), kNoAllocScratchBytes);
+  return rc;
 }

@@ -10,6 +10,7 @@ import contextlib
 import ctypes
 import functools
 import math
+import os
 from typing import Optional, Sequence, Tuple, Union
 
 import torch
@@ -18,6 +19,14 @@ from . import _lib
 from ._lib import check
 
 GROUP_SIZE = 64
+# Opt-in: read the device status word after every attention call (synchronizes the stream;
+# for debugging — the default reads it only when device_status()/check_device() is called).
+CHECK_EACH_CALL = bool(os.environ.get("CHAD_QKV_CHECK"))
+
+
+class DeviceWaitError(RuntimeError):
+    """A kernel gave up on a bounded wait (QKV_EDEVICE): its output is not trustworthy.
+    The cached workspaces of the device have been zeroed again, so later calls are."""
 _DT = {torch.bfloat16: _lib.QKV_BF16, torch.float16: _lib.QKV_F16, torch.float32: _lib.QKV_F32}
 
 QuantTuple = Tuple[torch.Tensor, torch.Tensor, torch.Tensor]
@@ -91,6 +100,27 @@ def quantize_append(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                                       scales.data_ptr(), biases.data_ptr(), b, h, s, d, np_,
                                       offset, bits, group_size, dtype_code(scales),
                                       _stream(dev)))
+
+
+def quantize_append_kv(k: torch.Tensor, v: torch.Tensor, k_quant: Sequence[torch.Tensor],
+                       v_quant: Sequence[torch.Tensor], offset: int, bits: int,
+                       group_size: int = GROUP_SIZE) -> None:
+    """Quantize k and v (B, H, S, D) into their cache buffers at [offset, offset+S), one
+    launch for both."""
+    dev = _need_cuda(k, v, *k_quant, *v_quant)
+    for t, nm in ((k, "k"), (v, "v"), *((t, "cache") for t in (*k_quant, *v_quant))):
+        _contig(t, nm)
+    if k.shape != v.shape or k.dtype != v.dtype:
+        raise ValueError("k and v must share shape and dtype")
+    b, h, s, d = k.shape
+    np_ = k_quant[0].shape[2]
+    kw, ks, kb = k_quant
+    vw, vs, vb = v_quant
+    with _on(dev):
+        check(_lib.load().qkv_quantize_append_kv(
+            k.data_ptr(), v.data_ptr(), dtype_code(k), kw.data_ptr(), ks.data_ptr(),
+            kb.data_ptr(), vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), b, h, s, d, np_, offset,
+            bits, group_size, dtype_code(ks), _stream(dev)))
 
 
 def quantize(x: torch.Tensor, bits: int, group_size: int = GROUP_SIZE,
@@ -231,6 +261,8 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
                                 _ptr(total_lens), bits, group_size, dtype_code(q), float(scale),
                                 kind, _ptr(m), mnk, sb, sh, sq, out_kind, splits,
                                 ws.data_ptr(), ws.numel(), _stream(dev)))
+        if CHECK_EACH_CALL:
+            check_device()
     return out
 
 
@@ -304,10 +336,33 @@ def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
             vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B, HQ, HKV, S, D, NP,
             offset, bits, group_size, dtype_code(q), float(scale), ws.data_ptr(), ws.numel(),
             _stream(dev)))
+        if CHECK_EACH_CALL:
+            check_device()
     return out
 
 
 def device_status(reset: bool = True) -> int:
-    """Device status word (0 = no kernel gave up on a bounded wait). Synchronizes."""
+    """Device status word of the current device (0 = no kernel gave up on a bounded wait).
+    Synchronizes torch's current stream. With reset, a non-zero word is cleared and every
+    workspace this module cached for the device is zeroed again (a merge that gave up may
+    have left partial words behind, which the next call would read as written); the library
+    zeroes the static scratch of qkv_attention_noalloc itself."""
     dev = torch.device("cuda", torch.cuda.current_device())
-    return int(_lib.load().qkv_device_status(_stream(dev), 1 if reset else 0))
+    v = int(_lib.load().qkv_device_status(_stream(dev), 1 if reset else 0))
+    if v < 0 and v > -1000:  # the call itself failed (not a status word)
+        check(v)
+    if v != 0 and reset:
+        ws = _WS.get((dev.type, dev.index))
+        if ws is not None:
+            ws.zero_()
+    return v
+
+
+def check_device() -> None:
+    """Raise DeviceWaitError if a kernel on the current device gave up on a bounded wait
+    since the last check (after resetting the status and zeroing the cached workspaces)."""
+    v = device_status(reset=True)
+    if v != 0:
+        raise DeviceWaitError(
+            f"a libqkv kernel gave up on a bounded wait (status {v}): outputs since the last "
+            "check are not trustworthy; the workspace has been zeroed")

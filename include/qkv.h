@@ -20,7 +20,9 @@
  *     call never synchronizes the device, so calls on one stream are reentrant;
  *   - the return value is a status: QKV_OK (0) or a negative QKV_E* code, never an abort;
  *     qkv_last_error() returns a human-readable message for the calling thread;
- *   - shapes use int, element strides long long; pointers must be 16-byte aligned.
+ *   - shapes use int, element strides long long; pointers must be 16-byte aligned;
+ *   - per-device state (symbol addresses, SM counts, occupancy) is looked up once per device
+ *     and kept for the life of the process: after cudaDeviceReset, restart the process.
  */
 #ifndef CHAD_B200_QKV_H
 #define CHAD_B200_QKV_H
@@ -62,8 +64,19 @@ int qkv_version(void);
 const char* qkv_last_error(void);
 
 /* Device-side status word: 0, or a QKV_EDEVICE code left by a kernel whose bounded
- * wait ran out. Synchronizes `stream`. reset != 0 clears the word afterwards. */
+ * wait ran out (every wait in the library gives up after about 2 s instead of hanging).
+ * Synchronizes `stream`. reset != 0 then clears the word and zeroes the static scratch of
+ * qkv_attention_noalloc on the current device (a merge that gave up may have left words
+ * behind). A caller-owned attention workspace is the caller's to zero again after a
+ * non-zero status. No counterpart in the reference (MLX kernels have no bounded waits). */
 int qkv_device_status(void* stream, int reset);
+
+/* Testing hooks (no counterpart in the reference), process-wide, 0 = off:
+ *   phantom_splits: decode merges wait for this many extra partial sets that no CTA
+ *                   writes, so their bounded wait runs out (the workspace must hold them);
+ *   spin_ns:        bound on that wait in nanoseconds instead of the default 2 s.
+ * Lets a test drive the timeout path (QKV_EDEVICE status, recovery) without a GPU fault. */
+int qkv_test_hooks(int phantom_splits, long long spin_ns);
 
 /*
  * Quantize S new rows per (b,h) and write them into the padded cache at positions
@@ -77,6 +90,16 @@ int qkv_device_status(void* stream, int reset);
 int qkv_quantize_append(const void* x, int x_dtype, void* w, void* scales, void* biases,
                         int B, int H, int S, int D, int NP, int offset, int bits,
                         int group_size, int scale_dtype, void* stream);
+
+/*
+ * K and V of the same S new rows in one launch: qkv_quantize_append on (k, kw, ks, kb) and
+ * on (v, vw, vs, vb), as mlx-lm's QuantizedKVCache.update_and_fetch quantizes both per call
+ * (tests/test_mlx_qsdpa.py:45-49). Same argument rules; k and v share x_dtype and shape.
+ */
+int qkv_quantize_append_kv(const void* k, const void* v, int x_dtype, void* kw, void* ks,
+                           void* kb, void* vw, void* vs, void* vb, int B, int H, int S, int D,
+                           int NP, int offset, int bits, int group_size, int scale_dtype,
+                           void* stream);
 
 /*
  * Dequantize `rows` packed rows of D values: the semantics of mx.dequantize as called at
@@ -176,7 +199,8 @@ int qkv_prefill(const void* q, const void* k_new, const void* v_new, void* kw, v
  * QKV_EWORKSPACE with a message naming both sizes. The first call on a device looks up the
  * array's address (cudaGetSymbolAddress) and should come before any stream capture. All
  * calls on a device share the array: calls that overlap on the GPU race, so serialize them.
- * Arguments and results are those of qkv_attention.
+ * After qkv_device_status reports QKV_EDEVICE, call qkv_device_status(stream, 1): it zeroes
+ * the array again. Arguments and results are those of qkv_attention.
  */
 int qkv_attention_noalloc(const void* q, const void* kw, const void* ks, const void* kb,
                           const void* vw, const void* vs, const void* vb, void* out, int B,

@@ -123,3 +123,19 @@ def test_python_workspace_estimate_covers_every_key_count(B, HQ, HKV, S, D, bits
     for n in list(range(1, 40000, 97)) + [8191, 8192, 8193, 8696, 16384, 16385, 131072]:
         assert ops.workspace_size(B, HQ, HKV, S, D, n, bits) >= \
             lib.qkv_workspace_size(B, HQ, HKV, S, D, n, bits, 64), n
+
+
+def test_test_hook_arguments_are_checked():
+    lib = _lib.load()
+    assert lib.qkv_test_hooks(-1, 0) == _lib.QKV_EINVAL
+    assert lib.qkv_test_hooks(0, -5) == _lib.QKV_EINVAL
+    assert lib.qkv_test_hooks(0, 0) == _lib.QKV_OK
+
+
+def test_kv_append_rejects_bad_arguments():
+    lib = _lib.load()
+    # offset + S beyond the padded length, then a bad x dtype
+    assert lib.qkv_quantize_append_kv(16, 16, 0, 16, 16, 16, 16, 16, 16, 1, 2, 10, 128, 8, 0, 4,
+                                      64, 0, None) == _lib.QKV_EINVAL
+    assert lib.qkv_quantize_append_kv(16, 16, 7, 16, 16, 16, 16, 16, 16, 1, 2, 1, 128, 8, 0, 4,
+                                      64, 0, None) == _lib.QKV_EINVAL
