@@ -269,6 +269,12 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     bulk_g2s(st + GG::OFF_VB, vb, sb, &full_bar[slot]);
   };
   int pre = 0;  // stages issued before the dependency wait
+  if (warp == kWarps && lane == 1 && !a.balanced) {
+    // Warm L2 with this CTA's query rows: the loads after the dependency wait then hit L2
+    // instead of queueing in HBM behind the KV stream. L2 is the point of coherence, so a
+    // predecessor that writes q after this hint still has its values read below.
+    prefetch_l2((const uint8_t*)a.q + (row0 + rbase) * D * 2, (uint32_t)(rows_here * D * 2));
+  }
   if (warp == kWarps && lane == 0 && !a.lens) {
     const int len0 = min(max(a.n, 0), a.NP);
     const int end0 = min(p_begin + a.chunk, len0);
@@ -373,25 +379,55 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
     // the same f16 values feed the bias term.
     uint32_t qf[NT][G][KS][2];
     float qsum_mine[NT][G];
+    uint4 raw[NT][G][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int r = rbase + nt * 8 + gq;
       const bool rv = r < R;
       const T* qr = qg + (row0 + (rv ? r : 0)) * D;
-      uint4 raw[G][2];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const uint4* src = reinterpret_cast<const uint4*>(qr + 64 * g + 16 * tq);
-        raw[g][0] = rv ? src[0] : make_uint4(0u, 0u, 0u, 0u);
-        raw[g][1] = rv ? src[1] : make_uint4(0u, 0u, 0u, 0u);
+        raw[nt][g][0] = rv ? src[0] : make_uint4(0u, 0u, 0u, 0u);
+        raw[nt][g][1] = rv ? src[1] : make_uint4(0u, 0u, 0u, 0u);
       }
+    }
+    // The f16 MMA operands hold q * scale * log2(e) times a power of two 2^-qsh chosen so
+    // that the largest magnitude among the CTA's query rows lands in [2^13, 2^14): any bf16
+    // q stays inside f16's range and small rows keep full precision. 2^qsh is folded back
+    // into the score's scale factor (kmul) and the bias sums (every warp loads the same
+    // rows, so qsh is the same in all of them).
+    float qmax = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t w4[4] = {raw[nt][g][hh].x, raw[nt][g][hh].y, raw[nt][g][hh].z,
+                                  raw[nt][g][hh].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            qmax = fmaxf(qmax, fmaxf(fabsf(Elem<T>::bits_to_f32((uint16_t)(w4[u] & 0xffffu))),
+                                     fabsf(Elem<T>::bits_to_f32((uint16_t)(w4[u] >> 16)))));
+        }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
+    qmax *= fabsf(qmul);
+    const int qsh = min(max((int)((__float_as_uint(qmax) >> 23) & 0xffu) - 127 - 13, -60), 100);
+    const float qmul_n = qmul * __uint_as_float((uint32_t)(127 - qsh) << 23);  // * 2^-qsh
+    const float kmul = __uint_as_float((uint32_t)(127 + 24 + qsh) << 23);      // 2^(24+qsh)
+    const float bmul = __uint_as_float((uint32_t)(127 + qsh) << 23);           // 2^qsh
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const uint32_t w[8] = {raw[g][0].x, raw[g][0].y, raw[g][0].z, raw[g][0].w,
-                               raw[g][1].x, raw[g][1].y, raw[g][1].z, raw[g][1].w};
+        const uint32_t w[8] = {raw[nt][g][0].x, raw[nt][g][0].y, raw[nt][g][0].z,
+                               raw[nt][g][0].w, raw[nt][g][1].x, raw[nt][g][1].y,
+                               raw[nt][g][1].z, raw[nt][g][1].w};
         auto qv = [&](int d) {  // dim d of the 16-dim slice, scaled, rounded to f16
           const uint32_t bitsv = (d & 1) ? (w[d >> 1] >> 16) : (w[d >> 1] & 0xffffu);
-          return __half2float(__float2half_rn(Elem<T>::bits_to_f32((uint16_t)bitsv) * qmul));
+          return __half2float(__float2half_rn(Elem<T>::bits_to_f32((uint16_t)bitsv) * qmul_n));
         };
         float acc = 0.f;
 #pragma unroll
@@ -417,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        qsum_mine[nt][g] = acc;  // for row nt*8 + gq
+        qsum_mine[nt][g] = acc * bmul;  // for row nt*8 + gq, in true (unshifted) units
       }
     }
     // this lane's score columns are rows 2*tq, 2*tq+1 of each n-tile
@@ -447,6 +483,12 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
       m_run[nt][0] = m_run[nt][1] = kNegInf;
       l_run[nt][0] = l_run[nt][1] = 0.f;
     }
+
+    // P * (V group scale) is an f16 MMA operand, with P <= 2^kLazyLog2: group scales above
+    // 2^11 would overflow it. This warp then scales its V operands by 2^-vsh (a power of
+    // two, raised as larger scales appear, with the accumulators rescaled to match) and
+    // multiplies the output back by 2^vsh. Ordinary data never takes that branch.
+    float vmul = 1.f;  // 2^-vsh
 
     const int kA = key_perm<BITS>(gq), kB = key_perm<BITS>(gq + 8);
     const int v0k = key_perm<BITS>(2 * tq), v1k = key_perm<BITS>(2 * tq + 1);
@@ -532,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
               float v = 0.f;
 #pragma unroll
               for (int g = 0; g < G; ++g) {
-                const float sc = (i < 2 ? ksA[g] : ksB[g]) * 16777216.0f;
+                const float sc = (i < 2 ? ksA[g] : ksB[g]) * kmul;
                 const float bi = i < 2 ? kbA[g] : kbB[g];
                 v = fmaf(sc, acc[h][nt][g][i], fmaf(bi, qsum[nt][i & 1][g], v));
               }
@@ -593,6 +635,43 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
 #pragma unroll
               for (int g = 0; g < G; ++g) vsB[h][g] = vbB[h][g] = 0.f;
             }
+          }
+        }
+        {
+          float vabs = 0.f;
+#pragma unroll
+          for (int h = 0; h < kSub; ++h)
+#pragma unroll
+            for (int g = 0; g < G; ++g) vabs = fmaxf(vabs, fmaxf(fabsf(vsA[h][g]), fabsf(vsB[h][g])));
+          if (__any_sync(0xffffffffu, vabs * vmul > 2048.f)) {
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1)
+              vabs = fmaxf(vabs, __shfl_xor_sync(0xffffffffu, vabs, off));
+            const int vsh = 127 - (int)(__float_as_uint(vmul) >> 23);
+            const int e = (int)((__float_as_uint(vabs) >> 23) & 0xffu) - 127;  // floor(log2)
+            const int ns = min(max(vsh, e - 10), 126);  // vabs * 2^-ns < 2^11
+            if (ns > vsh) {
+              const float r = __uint_as_float((uint32_t)(127 - (ns - vsh)) << 23);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int j = 0; j < G * KS; ++j) {
+                  o[nt][j][0] *= r;
+                  o[nt][j][1] *= r;
+                  o[nt][j][2] *= r;
+                  o[nt][j][3] *= r;
+                }
+              vmul = __uint_as_float((uint32_t)(127 - ns) << 23);
+            }
+          }
+          if (vmul != 1.f) {
+#pragma unroll
+            for (int h = 0; h < kSub; ++h)
+#pragma unroll
+              for (int g = 0; g < G; ++g) {
+                vsA[h][g] *= vmul;
+                vsB[h][g] *= vmul;
+              }
           }
         }
         uint32_t pf[kSub][NT][G][2];
@@ -766,15 +845,16 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         f[c] = ex2(m_run[nt][c] - (mx == kNegInf ? 0.f : mx));
         if (gq == 0) lw[warp * RG + r] = l_fin[nt][c] * f[c];
       }
+      const float vpow = __uint_as_float((uint32_t)(254u - (__float_as_uint(vmul) >> 23)) << 23);  // 2^vsh
 #pragma unroll
       for (int j = 0; j < G * KS; ++j) {
         const int g = j / KS;
         float4 v;
         const float shi = BITS == 4 ? 1048576.0f : 16777216.0f;  // 2^24 (/16 for x16 rows)
-        v.x = f[0] * fmaf(o[nt][j][0], 16777216.0f, obias[nt][0][g]);
-        v.y = f[1] * fmaf(o[nt][j][1], 16777216.0f, obias[nt][1][g]);
-        v.z = f[0] * fmaf(o[nt][j][2], shi, obias[nt][0][g]);
-        v.w = f[1] * fmaf(o[nt][j][3], shi, obias[nt][1][g]);
+        v.x = f[0] * fmaf(o[nt][j][0] * vpow, 16777216.0f, obias[nt][0][g]);
+        v.y = f[1] * fmaf(o[nt][j][1] * vpow, 16777216.0f, obias[nt][1][g]);
+        v.z = f[0] * fmaf(o[nt][j][2] * vpow, shi, obias[nt][0][g]);
+        v.w = f[1] * fmaf(o[nt][j][3] * vpow, shi, obias[nt][1][g]);
         reinterpret_cast<float4*>(ow + warp * RG * D)[(nt * G * KS + j) * 32 + lane] = v;
       }
     }

@@ -57,14 +57,24 @@ class ShardedDecoder:
     def step(self, qs: Sequence[torch.Tensor]) -> torch.Tensor:
         """qs: one query tensor (B, HQ, S, D) per layer. Returns (L, B, HQ, S, D)."""
         local = torch.stack([self.partial_fn(l, q) for l, q in enumerate(qs)])
+        return self.merge(local)
+
+    def gather(self, local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Every rank's partial rows: (world, *local.shape), one all_gather_into_tensor.
+        `out` (optional) is a preallocated buffer of that shape, reused across steps."""
         if self.world == 1:
-            gathered = local.unsqueeze(0)
-        else:
-            gathered = torch.empty((self.world, *local.shape), dtype=local.dtype,
-                                   device=local.device)
-            self.dist.all_gather_into_tensor(gathered.view(-1), local.contiguous().view(-1),
-                                            group=self.group)
-        return self.combine_fn(gathered)
+            return local.unsqueeze(0)
+        if out is None:
+            out = torch.empty((self.world, *local.shape), dtype=local.dtype,
+                              device=local.device)
+        self.dist.all_gather_into_tensor(out.view(-1), local.contiguous().view(-1),
+                                        group=self.group)
+        return out
+
+    def merge(self, local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Gather this rank's partial rows (any leading layer axes) with every other rank's
+        and merge them: the cross-GPU pass 2. Several layers may share the one gather."""
+        return self.combine_fn(self.gather(local, out))
 
 
 def gpu_partial_fn(caches, lens_local: torch.Tensor, pos_base: torch.Tensor,

@@ -56,8 +56,12 @@ import numpy as np
 def f32_to_bf16_bits(x) -> np.ndarray:
     """float32 -> bfloat16 bit pattern, round to nearest even (NaN -> canonical qNaN)."""
     x = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
-    u = x.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = x.view(np.uint32)
+    # finite values and infinities cannot carry out of 32 bits (at most 0xFF807FFF); NaN
+    # patterns may wrap, and are replaced below
+    with np.errstate(over="ignore"):
+        r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1)))
+             >> np.uint32(16)).astype(np.uint16)
     r[np.isnan(x)] = 0x7FC0
     return r
 
@@ -141,12 +145,16 @@ def affine_quantize(x, bits: int, group_size: int = 64, scale_dtype: str = "bf16
 
 def unpack_codes(w, bits: int) -> np.ndarray:
     """uint32 (..., W) -> integer codes (..., W*32/bits), LSB-first."""
-    w = np.asarray(w, dtype=np.uint32)
+    w = np.ascontiguousarray(np.asarray(w, dtype=np.uint32))
     per_word = 32 // bits
-    shifts = (np.arange(per_word, dtype=np.uint32) * bits).astype(np.uint32)
-    mask = np.uint32((1 << bits) - 1)
-    c = (w[..., None] >> shifts) & mask
-    return c.reshape(*w.shape[:-1], w.shape[-1] * per_word)
+    # little-endian bytes of a word are its elements in order (LSB-first packing)
+    by = w.astype("<u4", copy=False).view(np.uint8).reshape(*w.shape[:-1], w.shape[-1] * 4)
+    if bits == 8:
+        return by.astype(np.uint32)
+    c = np.empty((*w.shape[:-1], w.shape[-1] * per_word), dtype=np.uint32)
+    c[..., 0::2] = by & np.uint8(0xF)
+    c[..., 1::2] = by >> np.uint8(4)
+    return c
 
 
 def dequantize(w, scales, biases, bits: int, group_size: int = 64,
@@ -245,6 +253,55 @@ def attention_quantized_fp32(q, kq, vq, scale, lens, bits, group_size=64, mask=N
     k = dequantize_f32(*kq, bits, group_size, scale_dtype, round_mode)
     v = dequantize_f32(*vq, bits, group_size, scale_dtype, round_mode)
     return attention_fp32(q, k, v, scale, lens, mask)
+
+
+def attention_quantized_rows(q, kq, vq, scale, lens, bits, group_size=64,
+                             scale_dtype="bf16", q_pos=None, round_mode="fused",
+                             key_base=0):
+    """`attention_quantized_fp32` for long caches, one (batch, kv head) at a time.
+
+    Same arithmetic as ``attention_quantized_fp32`` (dequantize to the storage dtype, then
+    float32 attention, tests/test_mlx_qsdpa.py:52-65) but it dequantizes only the
+    ``lens[b]`` valid positions of one kv head at a time, so a 128K-key batch fits in a few
+    hundred MB. ``q_pos`` (B, S) int, optional: absolute position of each query row; row s
+    of batch b sees only keys at positions ``key_base + j <= q_pos[b, s]`` (the causal rule
+    of mlx_qsdpa.py:751-766 evaluated for an arbitrary subset of the new chunk's rows).
+    """
+    import concurrent.futures as cf
+    import os
+
+    q = np.asarray(q, np.float32)
+    b_, hq_, s_, d_ = q.shape
+    hkv = kq[0].shape[1]
+    gqa = hq_ // hkv
+    lens = [lens] * b_ if np.isscalar(lens) else list(lens)
+    out = np.zeros((b_, hq_, s_, d_), np.float32)
+
+    def one(bh):
+        b, h = bh
+        n = int(lens[b])
+        if n > 0:
+            k = dequantize_f32(kq[0][b, h, :n], kq[1][b, h, :n], kq[2][b, h, :n], bits,
+                               group_size, scale_dtype, round_mode)
+            v = dequantize_f32(vq[0][b, h, :n], vq[1][b, h, :n], vq[2][b, h, :n], bits,
+                               group_size, scale_dtype, round_mode)
+            qs = q[b, h * gqa:(h + 1) * gqa].reshape(gqa * s_, d_) * np.float32(scale)
+            sc = qs @ k.T  # (gqa*S, n)
+            if q_pos is not None:
+                pos = np.tile(np.asarray(q_pos[b]), gqa)[:, None]
+                sc = np.where(key_base + np.arange(n)[None, :] <= pos, sc, -np.inf)
+            mx = sc.max(axis=-1, keepdims=True)
+            ok = np.isfinite(mx)
+            e = np.where(ok, np.exp(sc - np.where(ok, mx, 0)), 0.0).astype(np.float32)
+            den = e.sum(axis=-1, keepdims=True)
+            p = np.where(den > 0, e / np.where(den > 0, den, 1), 0.0).astype(np.float32)
+            out[b, h * gqa:(h + 1) * gqa] = (p @ v).reshape(gqa, s_, d_)
+
+    # (numpy releases the GIL in the heavy array operations: threads share the work)
+    pairs = [(b, h) for b in range(b_) for h in range(hkv)]
+    with cf.ThreadPoolExecutor(max_workers=max(1, min(len(pairs), os.cpu_count() or 1, 16))) as ex:
+        list(ex.map(one, pairs))
+    return out
 
 
 def attention_stock(q, kq, vq, scale, lens, bits, group_size=64, mask=None,
