@@ -392,69 +392,66 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         raw[nt][g][1] = rv ? src[1] : make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    // The f16 MMA operands hold q * scale * log2(e) times a power of two 2^-qsh chosen so
-    // that the largest magnitude among the CTA's query rows lands in [2^13, 2^14): any bf16
-    // q stays inside f16's range and small rows keep full precision. 2^qsh is folded back
-    // into the score's scale factor (kmul) and the bias sums (every warp loads the same
-    // rows, so qsh is the same in all of them).
-    float qmax = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t w4[4] = {raw[nt][g][hh].x, raw[nt][g][hh].y, raw[nt][g][hh].z,
-                                  raw[nt][g][hh].w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            qmax = fmaxf(qmax, fmaxf(fabsf(Elem<T>::bits_to_f32((uint16_t)(w4[u] & 0xffffu))),
-                                     fabsf(Elem<T>::bits_to_f32((uint16_t)(w4[u] >> 16)))));
-        }
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
-    qmax *= fabsf(qmul);
-    const int qsh = min(max((int)((__float_as_uint(qmax) >> 23) & 0xffu) - 127 - 13, -60), 100);
-    const float qmul_n = qmul * __uint_as_float((uint32_t)(127 - qsh) << 23);  // * 2^-qsh
-    const float kmul = __uint_as_float((uint32_t)(127 + 24 + qsh) << 23);      // 2^(24+qsh)
-    const float bmul = __uint_as_float((uint32_t)(127 + qsh) << 23);           // 2^qsh
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const uint32_t w[8] = {raw[nt][g][0].x, raw[nt][g][0].y, raw[nt][g][0].z,
-                               raw[nt][g][0].w, raw[nt][g][1].x, raw[nt][g][1].y,
-                               raw[nt][g][1].z, raw[nt][g][1].w};
-        auto qv = [&](int d) {  // dim d of the 16-dim slice, scaled, rounded to f16
-          const uint32_t bitsv = (d & 1) ? (w[d >> 1] >> 16) : (w[d >> 1] & 0xffffu);
-          return __half2float(__float2half_rn(Elem<T>::bits_to_f32((uint16_t)bitsv) * qmul_n));
-        };
-        float acc = 0.f;
-#pragma unroll
-        for (int k = 0; k < KS; ++k) {
-          int d0, d1, d2, d3;
-          if constexpr (BITS == 4) {
-            const int u = k >> 1, h = k & 1;
-            d0 = 8 * u + 2 * h;
-            d1 = d0 + 4;
-            d2 = d0 + 1;
-            d3 = d0 + 5;
-          } else {
-            d0 = 4 * k;
-            d1 = d0 + 2;
-            d2 = d0 + 1;
-            d3 = d0 + 3;
+    // The f16 MMA operands hold q * scale * log2(e). A query whose products reach 2^14 (far
+    // beyond any activation a model produces, but possible in bf16) would leave f16's range:
+    // then, and only then, the CTA scales them by a power of two 2^-qsh that brings the
+    // largest magnitude of its rows into [2^13, 2^14), and folds 2^qsh back into the score's
+    // scale factor (kmul) and the bias sums. Every warp loads the same rows, so the decision
+    // and qsh are the same in all of them.
+    float lmax = 0.f;          // this lane's largest |q * scale * log2(e) * 2^-qsh|
+    float kmul = 16777216.0f;  // 2^(24+qsh)
+    float bmul = 1.f;          // 2^qsh
+    auto convert = [&](float qmul_n) {
+  #pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+  #pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const uint32_t w[8] = {raw[nt][g][0].x, raw[nt][g][0].y, raw[nt][g][0].z,
+                                 raw[nt][g][0].w, raw[nt][g][1].x, raw[nt][g][1].y,
+                                 raw[nt][g][1].z, raw[nt][g][1].w};
+          auto qv = [&](int d) {  // dim d of the 16-dim slice, scaled, rounded to f16
+            const uint32_t bitsv = (d & 1) ? (w[d >> 1] >> 16) : (w[d >> 1] & 0xffffu);
+            const float x = Elem<T>::bits_to_f32((uint16_t)bitsv) * qmul_n;
+            lmax = fmaxf(lmax, fabsf(x));
+            return __half2float(__float2half_rn(x));
+          };
+          float acc = 0.f;
+  #pragma unroll
+          for (int k = 0; k < KS; ++k) {
+            int d0, d1, d2, d3;
+            if constexpr (BITS == 4) {
+              const int u = k >> 1, h = k & 1;
+              d0 = 8 * u + 2 * h;
+              d1 = d0 + 4;
+              d2 = d0 + 1;
+              d3 = d0 + 5;
+            } else {
+              d0 = 4 * k;
+              d1 = d0 + 2;
+              d2 = d0 + 1;
+              d3 = d0 + 3;
+            }
+            const float v0 = qv(d0), v1 = qv(d1), v2 = qv(d2), v3 = qv(d3);
+            acc += (v0 + v1) + (v2 + v3);
+            const float hs = BITS == 4 ? 0.0625f : 1.f;
+            qf[nt][g][k][0] = pack_f16x2(v0, v1);
+            qf[nt][g][k][1] = pack_f16x2(v2 * hs, v3 * hs);
           }
-          const float v0 = qv(d0), v1 = qv(d1), v2 = qv(d2), v3 = qv(d3);
-          acc += (v0 + v1) + (v2 + v3);
-          const float hs = BITS == 4 ? 0.0625f : 1.f;
-          qf[nt][g][k][0] = pack_f16x2(v0, v1);
-          qf[nt][g][k][1] = pack_f16x2(v2 * hs, v3 * hs);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+          qsum_mine[nt][g] = acc * bmul;  // for row nt*8 + gq, in true (unshifted) units
         }
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        qsum_mine[nt][g] = acc * bmul;  // for row nt*8 + gq, in true (unshifted) units
       }
+    };
+    convert(qmul);
+    if (__any_sync(0xffffffffu, lmax >= 16384.f)) {
+      float qmax = lmax;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
+      const int qsh = min(max((int)((__float_as_uint(qmax) >> 23) & 0xffu) - 127 - 13, 0), 100);
+      kmul = __uint_as_float((uint32_t)(127 + 24 + qsh) << 23);
+      bmul = __uint_as_float((uint32_t)(127 + qsh) << 23);
+      convert(qmul * __uint_as_float((uint32_t)(127 - qsh) << 23));
     }
     // this lane's score columns are rows 2*tq, 2*tq+1 of each n-tile
     float qsum[NT][2][G];
@@ -845,16 +842,25 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         f[c] = ex2(m_run[nt][c] - (mx == kNegInf ? 0.f : mx));
         if (gq == 0) lw[warp * RG + r] = l_fin[nt][c] * f[c];
       }
+      // out = f * (2^vsh * 2^24 * o + obias) (2^20 for the x16 rows), one FMA per value
       const float vpow = __uint_as_float((uint32_t)(254u - (__float_as_uint(vmul) >> 23)) << 23);  // 2^vsh
+      const float shi = BITS == 4 ? 1048576.0f : 16777216.0f;
+      const float ka0 = 16777216.0f * vpow * f[0], ka1 = 16777216.0f * vpow * f[1];
+      const float kb0 = shi * vpow * f[0], kb1 = shi * vpow * f[1];
+      float ob0[G], ob1[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        ob0[g] = obias[nt][0][g] * f[0];
+        ob1[g] = obias[nt][1][g] * f[1];
+      }
 #pragma unroll
       for (int j = 0; j < G * KS; ++j) {
         const int g = j / KS;
         float4 v;
-        const float shi = BITS == 4 ? 1048576.0f : 16777216.0f;  // 2^24 (/16 for x16 rows)
-        v.x = f[0] * fmaf(o[nt][j][0] * vpow, 16777216.0f, obias[nt][0][g]);
-        v.y = f[1] * fmaf(o[nt][j][1] * vpow, 16777216.0f, obias[nt][1][g]);
-        v.z = f[0] * fmaf(o[nt][j][2] * vpow, shi, obias[nt][0][g]);
-        v.w = f[1] * fmaf(o[nt][j][3] * vpow, shi, obias[nt][1][g]);
+        v.x = fmaf(o[nt][j][0], ka0, ob0[g]);
+        v.y = fmaf(o[nt][j][1], ka1, ob1[g]);
+        v.z = fmaf(o[nt][j][2], kb0, ob0[g]);
+        v.w = fmaf(o[nt][j][3], kb1, ob1[g]);
         reinterpret_cast<float4*>(ow + warp * RG * D)[(nt * G * KS + j) * 32 + lane] = v;
       }
     }
