@@ -308,6 +308,25 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       vbi = ldg4((const uint8_t*)a.vb + sc0 + (long long)key * 4);
     }
   };
+  // Before the dependency wait: warm L2 with the first key tiles of this CTA's range that
+  // lie below a.prefetch_limit (cache positions the kernel just before does not write) and
+  // with its query rows. Only hints: L2 is the point of coherence, so anything the
+  // predecessor writes afterwards is still read correctly below.
+  if (warp == 4 && lane == 0) {
+    const int kend = min(min(k_stop, k_begin + 4 * kKT), a.prefetch_limit);
+    if (kend > k_begin) {
+      const uint32_t nk = (uint32_t)(kend - k_begin);
+      prefetch_l2(kw_base + (long long)k_begin * RB, nk * RB);
+      prefetch_l2(vw_base + (long long)k_begin * RB, nk * RB);
+      const uint32_t sb = (nk * 4u) & ~15u;  // whole 16-byte pieces inside the range
+      if (sb) {
+        prefetch_l2((const uint8_t*)a.ks + sc0 + (long long)k_begin * 4, sb);
+        prefetch_l2((const uint8_t*)a.kb + sc0 + (long long)k_begin * 4, sb);
+        prefetch_l2((const uint8_t*)a.vs + sc0 + (long long)k_begin * 4, sb);
+        prefetch_l2((const uint8_t*)a.vb + sc0 + (long long)k_begin * 4, sb);
+      }
+    }
+  }
   // barriers and tensor memory are set up; q, the cache (its newest positions may come from
   // the kernel just before) and the outputs are only touched after the predecessor is done
   asm volatile("griddepcontrol.wait;" ::: "memory");
