@@ -15,14 +15,16 @@ its own roofline, end-to-end number and CPU baseline: the 4-bit 32K decode, the 
 speculative-verify block over 16K keys, the 2048-token prefill over a 30720-token prefix,
 and the batch-4 ragged 64K-128K long-context decode.
 
-With N GPUs (torchrun, one process per GPU, NCCL) the sequences are sharded along the keys
+With N GPUs (torchrun, one process per GPU) the sequences are sharded along the keys
 (chad_b200.shard): every rank holds a contiguous range of each sequence, writes one (max,
-sum, out) partial row per query row per layer, and ShardedDecoder gathers the rows with
-one all_gather and merges them with the combine kernel. The headline keeps 32K keys per
-GPU (weak scaling, context 32K*N); the nested long-context line keeps the total work
-fixed (strong scaling, the same B4 64K-128K sequences split N ways), timed both with one
-gather per step (layers independent) and with a gather after every layer (a model that
-serialises its layers).
+sum, out) partial row per query row per layer, and ShardedDecoder merges the rows with one
+qkv_gather_combine launch per rank (each rank writes its rows into every rank's buffer over
+NVLink peer memory, waits for the others' and merges). The NCCL transport (one all_gather,
+then the combine kernel) is timed beside it. The headline keeps 32K keys per GPU (weak
+scaling, context 32K*N); the nested long-context line keeps the total work fixed (strong
+scaling, the same B4 64K-128K sequences split N ways), timed both with one merge per step
+(layers independent) and with a merge after every layer (a model that serialises its
+layers), over both transports.
 
 `value` = KV bytes read by all ranks per second (GB/s) for decode-type workloads, TFLOP/s
 for prefill. `e2e` repeats the step through the public API with pinned host buffers: the
@@ -299,7 +301,10 @@ def run_decode(args, name, cfg, rank, world, device):
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)  # the merge needs it zeroed
     keys_rank = sum(loc)  # this rank's keys per layer (all batch rows)
     kv_bytes_rank = keys_rank * HKV * kv_bytes_per_key(D, bits)
-    dec = ShardedDecoder() if sharded else None
+    # the step's merge: one qkv_gather_combine launch per rank (rows over NVLink peer
+    # memory); the NCCL all_gather + combine transport is timed beside it
+    dec = ShardedDecoder(transport="peer") if sharded else None
+    dec_nccl = ShardedDecoder() if sharded else None
 
     def attn(l, qq, n, lens, parts_out=None):
         c = caches[l]
@@ -319,7 +324,7 @@ def run_decode(args, name, cfg, rank, world, device):
     def step():
         graph.replay()
         if sharded:
-            dec.merge(part_local, gathered)
+            dec.merge(part_local, out)
 
     ms, clocks = _timed(step, args.steps, args.warmup, world, device)
 
@@ -345,14 +350,14 @@ def run_decode(args, name, cfg, rank, world, device):
     # per-layer gather (N > 1): attention -> all_gather -> combine after every layer, the
     # dependency chain of a model that serialises its layers; all 48 layers captured in one
     # CUDA graph with the collectives (eager launches if capture is refused)
-    per_layer = None
+    per_layer = step_nccl_res = None
     if sharded:
         gl = torch.empty((world, 1, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
 
         def per_layer_calls():
             for l in range(L):
                 attn(l, q[l], nloc, lens_t, part_local[l])
-                dec.merge(part_local[l:l + 1], gl)
+                dec_nccl.merge(part_local[l:l + 1], gl)
 
         how = "all layers captured in one CUDA graph with their NCCL all_gathers"
         gpl = None
@@ -376,6 +381,38 @@ def run_decode(args, name, cfg, rank, world, device):
                                     / (ms_pl * 1e-3) / 1e9, 2),
                      "how": how + "; max over ranks"}
         del gpl
+        torch.cuda.synchronize()
+
+        # the same chain with the peer-memory transport: one qkv_gather_combine kernel per
+        # layer writes the rows into every rank's buffer over NVLink and merges them
+        def per_layer_peer_calls():
+            for l in range(L):
+                attn(l, q[l], nloc, lens_t, part_local[l])
+                dec.merge(part_local[l:l + 1], out[l:l + 1])
+
+        gpp = _graph(per_layer_peer_calls, stream)
+        ms_pp, _ = _timed(gpp.replay, max(3, min(50, args.steps)), 2, world, device, clocks=False)
+        per_layer["peer"] = {
+            "ms_per_step": round(ms_pp, 5), "us_per_layer": round(ms_pp * 1e3 / L, 3),
+            "tok_per_s": round(B / (ms_pp * 1e-3), 1),
+            "value": round(_sum_over_ranks(kv_bytes_rank, world, device) * L
+                           / (ms_pp * 1e-3) / 1e9, 2),
+            "how": "all layers in one CUDA graph, a qkv_gather_combine launch after every "
+                   "decode_kernel launch (rows pushed over NVLink, no collective); max over ranks"}
+
+        # the step with the NCCL transport: one all_gather_into_tensor, then the combine
+        def step_nccl():
+            graph.replay()
+            dec_nccl.merge(part_local, gathered)
+
+        ms_sn, _ = _timed(step_nccl, max(3, min(50, args.steps)), 2, world, device,
+                          clocks=False)
+        step_nccl_res = {"ms_per_step": round(ms_sn, 5), "us_per_layer": round(ms_sn * 1e3 / L, 3),
+                         "value": round(_sum_over_ranks(kv_bytes_rank, world, device) * L
+                                        / (ms_sn * 1e-3) / 1e9, 2),
+                         "how": "the step's graph, then one NCCL all_gather_into_tensor and "
+                                "the combine kernel; max over ranks"}
+        del gpp
         torch.cuda.synchronize()
 
     # e2e through the public API with pinned host buffers
@@ -414,7 +451,7 @@ def run_decode(args, name, cfg, rank, world, device):
                               pos_base=base_t, total_lens=full_e2e, out=part_local[l],
                               out_kind=1, workspace=ws)
         if sharded:
-            hout.copy_(dec.merge(part_local, gathered).view_as(hout), non_blocking=True)
+            hout.copy_(dec.merge(part_local, out).view_as(hout), non_blocking=True)
         else:
             hout.copy_(out, non_blocking=True)
 
@@ -426,6 +463,8 @@ def run_decode(args, name, cfg, rank, world, device):
     d2h = hout.numel() * 2
     kv_bytes_all = _sum_over_ranks(kv_bytes_rank, world, device) * L
 
+    if dec is not None:
+        dec.close()
     del caches, graph
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -458,7 +497,8 @@ def run_decode(args, name, cfg, rank, world, device):
             "kv_bits": bits, "group_size": 64, "layers_per_step": L,
             "l2": f"inputs larger than L2: {L} distinct layer caches, "
                   f"{kv_bytes_rank * L / 1e9:.2f} GB per GPU",
-            "parallelism": (f"sequence-sharded split-KV x{world}, one all_gather per step"
+            "parallelism": (f"sequence-sharded split-KV x{world}, one qkv_gather_combine "
+                            "per step (partial rows over NVLink peer memory)"
                             if sharded else "single GPU"),
         },
         "roofline": {
@@ -482,6 +522,7 @@ def run_decode(args, name, cfg, rank, world, device):
     }
     if per_layer is not None:
         res["per_layer_gather"] = per_layer
+        res["step_merge_nccl"] = step_nccl_res
     return res
 
 

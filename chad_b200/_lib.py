@@ -24,6 +24,7 @@ QKV_EDEVICE = -6
 QKV_BF16, QKV_F16, QKV_F32 = 0, 1, 2
 QKV_MASK_NONE, QKV_MASK_CAUSAL, QKV_MASK_BOOL, QKV_MASK_ADDITIVE = 0, 1, 2, 3
 QKV_OUT_NORMALIZED, QKV_OUT_PARTIAL = 0, 1
+QKV_IPC_HANDLE_BYTES = 64  # size of a CUDA IPC memory handle (qkv_peer_alloc)
 
 # every symbol include/qkv.h declares, with (restype, argtypes)
 _vp, _i, _ll, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_size_t
@@ -66,6 +67,11 @@ SIGNATURES = {
          _i, _i, _vp],  # out_kind splits stream
     ),
     "qkv_combine": (_i, [_vp, _i, _ll, _i, _vp, _i, _i, _vp]),
+    "qkv_gather_buffer_size": (_sz, [_ll, _i, _i]),
+    "qkv_gather_combine": (_i, [_vp, _ll, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp]),
+    "qkv_peer_alloc": (_i, [_sz, _vp, _vp]),
+    "qkv_peer_open": (_i, [_vp, _vp]),
+    "qkv_peer_free": (_i, [_vp, _i]),
     "qkv_prefill": (
         _i,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

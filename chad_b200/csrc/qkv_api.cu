@@ -87,6 +87,8 @@ int num_sms() {
 
 size_t last_workspace_need() { return g_last_need; }
 
+int* device_status_word() { return status_ptr(); }
+
 int set_last_error(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);

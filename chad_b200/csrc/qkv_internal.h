@@ -134,6 +134,10 @@ int launch_prefill_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStre
 // arguments were valid enough to plan the launch).
 size_t last_workspace_need();
 
+// Device address of the status word (qkv_device_status) on the current device; nullptr if
+// it cannot be resolved.
+int* device_status_word();
+
 // Record a message for qkv_last_error() on this thread and return `code`.
 int set_last_error(int code, const char* fmt, ...);
 

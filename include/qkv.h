@@ -176,6 +176,36 @@ int qkv_combine(const float* parts, int n_parts, long long rows, int D, void* ou
                 int out_dtype, int out_kind, void* stream);
 
 /*
+ * Cross-GPU merge of sequence shards over peer memory, one kernel per rank: the rank's
+ * partial rows (`parts`, rows x (D+4) floats, QKV_OUT_PARTIAL layout, e.g. qkv_attention's
+ * output over its key shard) are written straight into every rank's receive buffer over
+ * NVLink, each float paired with the call's flag in one 64-bit word; the kernel then reads
+ * every rank's rows of this call as they land (bounded wait) and merges them with the pass-2
+ * rule of src/chad/mlx_qsdpa.py:233-258 into `out` (QKV_OUT_NORMALIZED: rows x D in
+ * out_dtype; QKV_OUT_PARTIAL: one merged partial row each). Replaces an all_gather
+ * collective plus qkv_combine; every rank calls it in the same order with the same rows.
+ *   peer_bufs: device array of `world` pointers, rank p's receive buffer as mapped in this
+ *              process (e.g. by CUDA IPC); my_buf = peer_bufs[rank]
+ *   buffers:   qkv_gather_buffer_size(rows, D, world) bytes each, zero before the first
+ *              call; their call counters only grow, so no host-side epoch is needed. After
+ *              a wait gave up (qkv_device_status), zero every rank's buffer again with every
+ *              rank idle before relying on the merge.
+ */
+size_t qkv_gather_buffer_size(long long rows, int D, int world);
+/* Receive buffers for qkv_gather_combine: qkv_peer_alloc makes a zeroed device buffer on
+ * the current device and, when ipc_handle is non-null, writes its QKV_IPC_HANDLE_BYTES
+ * CUDA IPC handle there for the other ranks; qkv_peer_open maps a peer's buffer from its
+ * handle; qkv_peer_free releases either (opened = 1 for a mapping). Free the own buffer
+ * only after every peer has closed its mapping of it. */
+#define QKV_IPC_HANDLE_BYTES 64
+int qkv_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int qkv_peer_open(const void* ipc_handle, void** ptr);
+int qkv_peer_free(void* ptr, int opened);
+int qkv_gather_combine(const float* parts, long long rows, int D, void* const* peer_bufs,
+                       void* my_buf, int world, int rank, void* out, int out_dtype,
+                       int out_kind, void* stream);
+
+/*
  * Prefill over the prefix cache: quantize-append the S new tokens' K/V at [offset,
  * offset+S) (the cache quantizes before attention runs, src/chad/engine.py:941-990), then
  * attend the S queries over all offset+S keys, causal within the new chunk.

@@ -139,3 +139,31 @@ def test_kv_append_rejects_bad_arguments():
                                       64, 0, None) == _lib.QKV_EINVAL
     assert lib.qkv_quantize_append_kv(16, 16, 7, 16, 16, 16, 16, 16, 16, 1, 2, 1, 128, 8, 0, 4,
                                       64, 0, None) == _lib.QKV_EINVAL
+
+
+def test_gather_buffer_size_and_argument_checks():
+    lib = _lib.load()
+    rows, D, W = 96, 128, 4
+    # data [2][world][rows][D+4] 64-bit words (flag, float), seen [rows] u32
+    assert lib.qkv_gather_buffer_size(rows, D, W) == 2 * W * rows * (D + 4) * 8 + rows * 4
+    assert lib.qkv_gather_buffer_size(rows, 100, W) == 0
+    assert lib.qkv_gather_buffer_size(0, D, W) == 0
+    E = _lib.QKV_EINVAL
+
+    def call(parts=16, n=rows, d=D, peers=16, mine=16, world=2, rank=0, out=16, dt=0, kind=0):
+        return lib.qkv_gather_combine(parts, n, d, peers, mine, world, rank, out, dt, kind, None)
+
+    assert call(parts=None) == E
+    assert call(peers=None) == E
+    assert call(rank=2) == E
+    assert call(world=0) == E
+    assert call(world=129, rank=0) == E
+    assert call(n=0) == E
+    assert call(d=100) == _lib.QKV_EUNSUPPORTED
+    assert call(dt=2) == E
+    assert call(kind=3) == E
+    assert call(parts=8) == _lib.QKV_EALIGN
+    p = ctypes.c_void_p()
+    assert lib.qkv_peer_alloc(0, ctypes.byref(p), None) == E
+    assert lib.qkv_peer_open(None, ctypes.byref(p)) == E
+    assert lib.qkv_peer_free(None, 0) == _lib.QKV_OK

@@ -122,3 +122,15 @@ def test_failed_rank_surfaces_as_error_not_hang():
     res = _run(2, fail_rank=1)
     assert res[1].startswith("error")
     assert res[0].startswith("error")  # the peer's collective errors out (timeout / abort)
+
+
+def test_transport_choice_is_checked():
+    from chad_b200.shard import ShardedDecoder
+
+    with pytest.raises(ValueError):
+        ShardedDecoder(transport="shm")
+    dec = ShardedDecoder(transport="peer")  # no process group: one rank, nothing to merge
+    assert dec.world == 1 and dec.transport == "peer"
+    local = torch.zeros((2, 1, 4, 1, 68))
+    assert dec.gather(local).shape == (1, 2, 1, 4, 1, 68)
+    dec.close()
