@@ -15,7 +15,7 @@ struct TcPlan {
   int tblocks;          // CTAs along the query tokens
   int splits;           // CTAs along the keys
   int chunk;            // keys per split (multiple of the 128-key tile)
-  int parts;            // partial rows per output row (splits, x2 when tiles == 1)
+  int parts;            // partial rows per output row (= splits)
   int parts_bound;      // parts at the requested split count, >= parts; unlike parts (whose
                         // chunk rounding can lower it) it never decreases as n grows
 };

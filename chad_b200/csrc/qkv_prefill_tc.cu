@@ -228,8 +228,8 @@ __device__ __forceinline__ uint32_t ldg4(const void* p) {
 
 // SK ("key-split tiles", MT == 2): the CTA's query rows fit one 128-row tile; both
 // tensor-memory tiles hold those rows and take alternate key tiles (tile m: keys tiles
-// m, m+2, ...), so one tile's softmax still overlaps the other's MMAs. Each tile writes its
-// own partial rows (partial 2*split + m).
+// m, m+2, ...), so one tile's softmax still overlaps the other's MMAs. The epilogue folds
+// tile 1 into tile 0: one partial row per query row and split.
 template <typename T, int BITS, int MT, bool SK>
 __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_constant__ TcParams P) {
   static_assert(!SK || MT == 2, "key-split tiles need both tensor-memory tiles");
@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   __shared__ uint64_t s_full[MT], p_full[MT], o_done[MT];
   __shared__ uint64_t mma_fin;
   __shared__ uint32_t tmem_sh;
+  __shared__ float sk_m[SK ? 128 : 1], sk_l[SK ? 128 : 1];  // tile 1's row state (SK)
 
   const AttnArgs& a = P.a;
   // Programmatic dependent launch: the next kernel may be scheduled once every CTA of this
@@ -635,10 +636,32 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
       ok = mbar_wait(&o_done[m], (my_tiles - 1) & 1, a.status, 47);
       ok = __all_sync(0xffffffffu, ok);
     }
-    if (ok) {
+    // SK: both tensor-memory tiles hold the same query rows over alternate key tiles. Tile 1
+    // hands its (max, sum) over through shared memory and tile 0 folds tile 1's O into its
+    // own (the warps 4 + j and 8 + j share tensor-memory lanes), so the CTA writes one
+    // partial row per query row, or the normalized output when it is the only split.
+    float f0 = 1.f, f1 = 0.f;
+    bool has1 = false;
+    if constexpr (SK) {
+      if (m == 1) {
+        sk_m[r] = m_run;
+        sk_l[r] = l_run;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+      has1 = ntiles > 1;
+      if (m == 0 && has1) {
+        const float m1 = sk_m[r], mx = fmaxf(m_run, m1);
+        const float mu = mx == kNegInfTc ? 0.f : mx;
+        f0 = ex2(m_run - mu);
+        f1 = ex2(m1 - mu);
+        l_run = fmaf(f0, l_run, f1 * sk_l[r]);
+        m_run = mx;
+      }
+    }
+    if (ok && !(SK && m == 1)) {
       tc::fence_after_sync();
       const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
-      const int part = SK ? 2 * split + m : split;
+      const int part = split;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
       for (int qd = 0; qd < 4; ++qd) {
@@ -648,6 +671,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) x[e] = 0u;
+        }
+        if (SK && has1) {
+          uint32_t y[32];
+          tc::ld32(to + 128 + qd * 32, y);
+          tc::wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            x[e] = __float_as_uint(fmaf(f0, __uint_as_float(x[e]), f1 * __uint_as_float(y[e])));
         }
         // column position p of an 8-dim group holds dim perm[p] (4-bit) or p (8-bit)
         float o[32];
@@ -813,8 +844,8 @@ TcPlan prefill_tc_plan(int B, int HQ, int HKV, int S, int n_max, int want_splits
   }
   p.chunk = ((n + best - 1) / best + kKT - 1) / kKT * kKT;
   p.splits = (n + p.chunk - 1) / p.chunk;
-  p.parts = p.splits * (p.tiles == 1 ? 2 : 1);
-  p.parts_bound = best * (p.tiles == 1 ? 2 : 1);
+  p.parts = p.splits;
+  p.parts_bound = best;
   return p;
 }
 

@@ -153,7 +153,8 @@ def test_verify_block_shape(bits):
 
 def test_key_split_tiles_partials():
     """A block that fits one 128-row tile runs its keys on both tensor-memory tiles
-    alternately: each split yields two partial rows per query row."""
+    alternately and the epilogue folds tile 1 into tile 0: one partial row per query row
+    per split, and the normalized output directly when there is one split."""
     from chad_b200 import ops
 
     S, n = 8, 2500 + 8
@@ -161,7 +162,19 @@ def test_key_split_tiles_partials():
     c = _cache(k, v, 4, "bf16")
     tq = torch_from_f32(q, "bf16")
     parts = ops.partials(tq, c.keys, c.values, 128 ** -0.5, n, 4, mask="causal", splits=3)
-    assert parts.shape[0] == 6
+    assert parts.shape[0] == 3
     ref = _ref(q, k, v, 4, "bf16", n, "causal")
     _check(ops.combine(parts.contiguous(), torch.bfloat16), ref)
     _check(_run(q, c, n, 4, "bf16", "causal", splits=1), ref)
+
+
+@pytest.mark.parametrize("n", [8, 100, 128 + 8, 256 + 8, 300])
+def test_key_split_tiles_with_one_or_two_key_tiles(n):
+    """Key ranges of one tile (tile 1 has no keys and is left out of the fold) and of two or
+    three tiles, 8- and 4-bit, one split (direct output)."""
+    S = 8
+    for bits in (4, 8):
+        q, k, v = make_case(93 + n, 1, 32, 4, S, 128, n, "bf16", outliers=True)
+        c = _cache(k, v, bits, "bf16")
+        _check(_run(q, c, n, bits, "bf16", "causal", splits=1),
+               _ref(q, k, v, bits, "bf16", n, "causal"))
