@@ -266,6 +266,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   const int lim_hi = causal ? n - a.S + t_last : n - 1;  // last key any row may see
   const int k_stop = min(min(k_begin + P.chunk, n), lim_hi + 1);
   const int ntiles = k_stop > k_begin ? (k_stop - k_begin + kKT - 1) / kKT : 0;
+  // softmax warps of a tile that hold query rows: a verify block packs its GQA x S rows into
+  // the first lanes (TT = S), and the warps past them sit the loop out
+  const int n_act = SK ? min(4, (gqa * TT + 31) / 32) : 4;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -276,7 +279,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     }
     for (int m = 0; m < MT; ++m) {
       mbar_init(&s_full[m], 1);
-      mbar_init(&p_full[m], 4);
+      mbar_init(&p_full[m], n_act);
       mbar_init(&o_done[m], 1);
     }
     mbar_init(&mma_fin, 1);
@@ -478,7 +481,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     const int hl = r / TT, t = t0 + (SK ? 0 : m) * TT + (r % TT);
     const bool row_ok = hl < gqa && t < a.S;
     // this tile's key tiles: all (SK = false) or m, m+2, ... (SK)
-    const int my_tiles = SK ? (ntiles > m ? (ntiles - m + 1) / 2 : 0) : ntiles;
+    const bool idle = SK && (warp & 3) >= n_act;
+    const int my_tiles = idle ? 0 : SK ? (ntiles > m ? (ntiles - m + 1) / 2 : 0) : ntiles;
     int lim = causal ? n - a.S + t : n - 1;
     lim = min(lim, k_stop - 1);
     const float c = a.scale * 1.4426950408889634f;
@@ -647,7 +651,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         sk_m[r] = m_run;
         sk_l[r] = l_run;
       }
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+      named_bar_sync(1, 256);  // the eight softmax warps
       has1 = ntiles > 1;
       if (m == 0 && has1) {
         const float m1 = sk_m[r], mx = fmaxf(m_run, m1);
@@ -658,7 +662,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         m_run = mx;
       }
     }
-    if (ok && !(SK && m == 1)) {
+    if (ok && !(SK && m == 1) && !idle) {
       tc::fence_after_sync();
       const long long row = ((long long)b * a.HQ + hkv * gqa + hl) * a.S + t;
       const int part = split;
@@ -761,7 +765,7 @@ int launch_tc(const AttnArgs& a, const TcPlan& p, bool combine, cudaStream_t st)
   using SM = TcSmem<MT>;
   TcParams prm;
   prm.a = a;
-  prm.TT = p.tokens_per_tile;
+  prm.TT = p.tiles == 1 ? std::min(p.tokens_per_tile, a.S) : p.tokens_per_tile;
   prm.chunk = p.chunk;
   const bool direct = combine && p.parts == 1 && a.out_kind == QKV_OUT_NORMALIZED;
   prm.parts = direct ? nullptr : reinterpret_cast<float*>(a.workspace);
