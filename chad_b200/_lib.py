@@ -80,7 +80,12 @@ SIGNATURES = {
 }
 
 _lib = None
+_ext = None
 _lock = threading.Lock()
+# entry points with CPython bindings (chad_b200._qkvext): the per-layer calls
+EXT_BOUND = {"qkv_attention": "attention", "qkv_prefill": "prefill",
+             "qkv_quantize_append_kv": "quantize_append_kv", "qkv_combine": "combine",
+             "qkv_gather_combine": "gather_combine"}
 
 
 class QKVError(RuntimeError):
@@ -105,8 +110,37 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
+            _bind_ext(lib)
             _lib = lib
     return _lib
+
+
+def _bind_ext(lib) -> None:
+    """Point the CPython bindings at this library instance (same ABI as the ctypes table,
+    a fraction of its per-call cost); without them every call goes through ctypes."""
+    global _ext
+    try:
+        from . import _qkvext
+    except ImportError:
+        _ext = None
+        return
+    for name in EXT_BOUND:
+        _qkvext.bind(name, ctypes.cast(getattr(lib, name), ctypes.c_void_p).value)
+    _ext = _qkvext
+
+
+def fn(name: str):
+    """The callable for entry point `name`: its CPython binding when built, else ctypes."""
+    lib = load()
+    if _ext is not None and name in EXT_BOUND:
+        return getattr(_ext, EXT_BOUND[name])
+    return getattr(lib, name)
+
+
+def ext():
+    """The CPython bindings module bound to the loaded library, or None if not built."""
+    load()
+    return _ext
 
 
 def check(rc: int) -> None:

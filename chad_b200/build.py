@@ -4,7 +4,8 @@
     python -m chad_b200.build --force  # rebuild everything
 
 Translation units compile in parallel to objects under chad_b200/_build/, then link into
-chad_b200/libqkv.so (static CUDA runtime, no torch dependency).
+chad_b200/libqkv.so (static CUDA runtime, no torch dependency). The CPython bindings of the
+per-layer entry points (csrc/qkv_pyext.c) build with gcc into chad_b200/_qkvext*.so.
 """
 
 from __future__ import annotations
@@ -64,9 +65,38 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_ext(force)
     if verbose:
         print(LIB)
     return LIB
+
+
+EXT_SRC = os.path.join(CSRC, "qkv_pyext.c")
+
+
+def ext_path() -> str:
+    import sysconfig
+
+    return os.path.join(HERE, "_qkvext" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_ext(force: bool = False) -> str:
+    """The CPython bindings of the per-layer entry points (chad_b200._qkvext), with gcc."""
+    import sysconfig
+
+    out = ext_path()
+    deps = [EXT_SRC, os.path.join(os.path.dirname(HERE), "include", "qkv.h"), __file__]
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= max(map(os.path.getmtime, deps)):
+        return out
+    cc = os.environ.get("CC") or shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("no C compiler for the Python bindings")
+    cmd = [cc, "-O2", "-fPIC", "-shared", "-std=gnu11", "-Wall",
+           "-I" + sysconfig.get_paths()["include"], EXT_SRC, "-o", out]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"bindings build failed:\n{r.stdout}\n{r.stderr}")
+    return out
 
 
 if __name__ == "__main__":

@@ -117,7 +117,7 @@ def quantize_append_kv(k: torch.Tensor, v: torch.Tensor, k_quant: Sequence[torch
     kw, ks, kb = k_quant
     vw, vs, vb = v_quant
     with _on(dev):
-        check(_lib.load().qkv_quantize_append_kv(
+        check(_lib.fn("qkv_quantize_append_kv")(
             k.data_ptr(), v.data_ptr(), dtype_code(k), kw.data_ptr(), ks.data_ptr(),
             kb.data_ptr(), vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), b, h, s, d, np_, offset,
             bits, group_size, dtype_code(ks), _stream(dev)))
@@ -248,14 +248,13 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
     for t in (lens, pos_base, total_lens):
         if t is not None and t.dtype != torch.int32:
             raise TypeError("lens/pos_base/total_lens must be int32")
-    lib = _lib.load()
     need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size, dev.index)
     if splits:
         # forced split count: rows of at most D + 16 floats per split (D + 2*D/32 merged)
         need = max(need, splits * B * HQ * S * (D + 16) * 4 + (1 << 16))
     ws = workspace if workspace is not None else _workspace(dev, need)
     with _on(dev):
-        check(lib.qkv_attention(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
+        check(_lib.fn("qkv_attention")(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
                                 vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(),
                                 B, HQ, HKV, S, D, NP, n, _ptr(lens), _ptr(pos_base),
                                 _ptr(total_lens), bits, group_size, dtype_code(q), float(scale),
@@ -309,7 +308,7 @@ def combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
     else:
         out = torch.empty(parts.shape[1:], dtype=torch.float32, device=parts.device)
     with _on(dev):
-        check(_lib.load().qkv_combine(parts.data_ptr(), p, rows, d, out.data_ptr(),
+        check(_lib.fn("qkv_combine")(parts.data_ptr(), p, rows, d, out.data_ptr(),
                                       dtype_code(out_dtype), out_kind, _stream(dev)))
     return out
 
@@ -330,7 +329,7 @@ def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size, dev.index)
     ws = _workspace(dev, need)
     with _on(dev):
-        check(_lib.load().qkv_prefill(
+        check(_lib.fn("qkv_prefill")(
             _contig(q, "q").data_ptr(), _contig(k_new, "k_new").data_ptr(),
             _contig(v_new, "v_new").data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
             vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B, HQ, HKV, S, D, NP,

@@ -99,7 +99,7 @@ class PeerGather:
                               device=local.device)
         code = ops.dtype_code(out_dtype)
         with ops._on(local.device):
-            _lib.check(_lib.load().qkv_gather_combine(
+            _lib.check(_lib.fn("qkv_gather_combine")(
                 local.data_ptr(), self.rows, self.D, self.peer_ptrs.data_ptr(), self._own,
                 self.world, self.rank, out.data_ptr(), code, out_kind,
                 ops._stream(local.device)))

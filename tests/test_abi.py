@@ -167,3 +167,26 @@ def test_gather_buffer_size_and_argument_checks():
     assert lib.qkv_peer_alloc(0, ctypes.byref(p), None) == E
     assert lib.qkv_peer_open(None, ctypes.byref(p)) == E
     assert lib.qkv_peer_free(None, 0) == _lib.QKV_OK
+
+
+def test_python_bindings_match_the_ctypes_table():
+    """The CPython bindings of the per-layer calls are built, bound to the loaded library,
+    and return the library's own status codes (argument checks run before any GPU work)."""
+    ext = _lib.ext()
+    assert ext is not None, "chad_b200._qkvext was not built"
+    for name, attr in _lib.EXT_BOUND.items():
+        assert _lib.fn(name) is getattr(ext, attr)
+    lib = _lib.load()
+    args = (16, 16, 16, 16, 16, 16, 16, 16, 1, 32, 4, 1, 100, 512, 10, None, None, None, 4, 64,
+            0, 0.1, 0, None, 0, 0, 0, 0, 0, 0, 16, 1 << 20, None)  # head_dim 100
+    assert ext.attention(*args) == lib.qkv_attention(*args) == _lib.QKV_EUNSUPPORTED
+    bad_kind = args[:28] + (7,) + args[29:]
+    assert ext.attention(*bad_kind) == lib.qkv_attention(*bad_kind) == _lib.QKV_EINVAL
+    assert ext.combine(None, 2, 4, 128, 16, 0, 0, None) == _lib.QKV_EINVAL
+    assert ext.gather_combine(None, 4, 128, 16, 16, 2, 0, 16, 0, 0, None) == _lib.QKV_EINVAL
+    assert ext.quantize_append_kv(16, 16, 7, 16, 16, 16, 16, 16, 16, 1, 2, 1, 128, 8, 0, 4, 64,
+                                  0, None) == _lib.QKV_EINVAL
+    with pytest.raises(TypeError):
+        ext.attention(*args[:-1])
+    with pytest.raises(OverflowError):
+        ext.combine(None, 1 << 40, 4, 128, 16, 0, 0, None)
