@@ -1000,20 +1000,44 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
         }
         mt = mx;
       }
-      xm[slot * kMergeCols + q4] = mt;
-      xl[slot * kMergeCols + q4] = lt;
-      reinterpret_cast<float4*>(xo)[slot * kMergeCols + q4] = acc;
+      // the warp's four slots of each column fold through shuffles (lanes 8 and 16 apart)
+#pragma unroll
+      for (int sh = 8; sh <= 16; sh *= 2) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, mt, sh);
+        const float l2 = __shfl_xor_sync(0xffffffffu, lt, sh);
+        float4 a2;
+        a2.x = __shfl_xor_sync(0xffffffffu, acc.x, sh);
+        a2.y = __shfl_xor_sync(0xffffffffu, acc.y, sh);
+        a2.z = __shfl_xor_sync(0xffffffffu, acc.z, sh);
+        a2.w = __shfl_xor_sync(0xffffffffu, acc.w, sh);
+        const float mx = fmaxf(mt, m2);
+        const float mu = mx == kNegInf ? 0.f : mx;
+        const float f1 = ex2(mt - mu), f2 = ex2(m2 - mu);
+        lt = fmaf(f1, lt, f2 * l2);
+        acc.x = fmaf(f1, acc.x, f2 * a2.x);
+        acc.y = fmaf(f1, acc.y, f2 * a2.y);
+        acc.z = fmaf(f1, acc.z, f2 * a2.z);
+        acc.w = fmaf(f1, acc.w, f2 * a2.w);
+        mt = mx;
+      }
+      if ((threadIdx.x & 31) < kMergeCols) {
+        const int w = threadIdx.x >> 5;
+        xm[w * kMergeCols + q4] = mt;
+        xl[w * kMergeCols + q4] = lt;
+        reinterpret_cast<float4*>(xo)[w * kMergeCols + q4] = acc;
+      }
     }
     __syncthreads();
     if (slot == 0) {
+      constexpr int kWarpsAll = kThreads / 32;
       float mx = kNegInf;
 #pragma unroll
-      for (int k = 0; k < kMergeSlots; ++k) mx = fmaxf(mx, xm[k * kMergeCols + q4]);
+      for (int k = 0; k < kWarpsAll; ++k) mx = fmaxf(mx, xm[k * kMergeCols + q4]);
       const float mu = mx == kNegInf ? 0.f : mx;
       float l = 0.f;
       float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int k = 0; k < kMergeSlots; ++k) {
+      for (int k = 0; k < kWarpsAll; ++k) {
         const float f = ex2(xm[k * kMergeCols + q4] - mu);
         const float4 v = reinterpret_cast<const float4*>(xo)[k * kMergeCols + q4];
         l = fmaf(f, xl[k * kMergeCols + q4], l);

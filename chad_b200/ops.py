@@ -54,17 +54,26 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+_DEVICES = {}
+
+
 def _need_cuda(*ts: torch.Tensor) -> torch.device:
-    dev = None
+    idx = None
     for t in ts:
         if t is None:
             continue
-        if not t.is_cuda:
+        d = t.get_device()  # -1 on the CPU; an int compare is cheaper than torch.device objects
+        if d < 0:
             raise ValueError("libqkv operates on CUDA tensors only")
-        if dev is None:
-            dev = t.device
-        elif t.device != dev:
+        if idx is None:
+            idx = d
+        elif d != idx:
             raise ValueError("tensors are on different devices")
+    if idx is None:
+        return None
+    dev = _DEVICES.get(idx)
+    if dev is None:
+        dev = _DEVICES[idx] = torch.device("cuda", idx)
     return dev
 
 
@@ -166,9 +175,7 @@ def workspace_size(B: int, HQ: int, HKV: int, S: int, D: int, n_max: int, bits: 
     hits the memoized value instead of calling into the library every step."""
     if device is None:
         device = torch.cuda.current_device() if torch.cuda.is_available() else -1
-    n = 256
-    while n < n_max:
-        n *= 2
+    n = max(256, 1 << (max(n_max, 1) - 1).bit_length())  # next power of two, at least 256
     return _workspace_size(device, B, HQ, HKV, S, D, n, bits, group_size)
 
 
