@@ -1072,7 +1072,42 @@ __global__ void __launch_bounds__(kThreads, DecodeCfg<BITS, D, NT>::CTAS) decode
 constexpr int kCombineWarps = 8;
 constexpr int kCombineBatch = 10;  // 80 partials per pass: a verify block's key splits in one
 
-template <typename TO, int D>
+// E consecutive floats at p (16-byte aligned when VEC): vector loads keep the LSU queue short
+template <int E, bool VEC>
+__device__ __forceinline__ void load_cols(const float* p, float* o) {
+  if constexpr (VEC && E % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < E / 4; ++i) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(p) + i);
+      o[4 * i] = v.x;
+      o[4 * i + 1] = v.y;
+      o[4 * i + 2] = v.z;
+      o[4 * i + 3] = v.w;
+    }
+  } else if constexpr (VEC && E == 2) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(p));
+    o[0] = v.x;
+    o[1] = v.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = __ldcg(p + e);
+  }
+}
+
+template <int E, bool VEC>
+__device__ __forceinline__ void zero_cols(float* p) {
+  if constexpr (VEC && E % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < E / 4; ++i) reinterpret_cast<float4*>(p)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else if constexpr (VEC && E == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(0.f, 0.f);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) p[e] = 0.f;
+  }
+}
+
+template <typename TO, int D, bool VEC>
 __global__ void __launch_bounds__(kCombineWarps * 32)
     combine_kernel(const float* parts, int n_parts, long long part_stride_rows, long long rows,
                    TO* __restrict__ out, float* __restrict__ out_part, float* clear) {
@@ -1097,10 +1132,15 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
       const int p = p0 + warp + k * kCombineWarps;
       if (p < n_parts) {
         const float* pr = base + p * pstride;
-        pm[k] = __ldcg(pr + D);
-        pl[k] = __ldcg(pr + D + 1);
-#pragma unroll
-        for (int e = 0; e < E; ++e) po[k][e] = __ldcg(pr + lane * E + e);
+        if constexpr (VEC) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(pr + D));
+          pm[k] = ml.x;
+          pl[k] = ml.y;
+        } else {
+          pm[k] = __ldcg(pr + D);
+          pl[k] = __ldcg(pr + D + 1);
+        }
+        load_cols<E, VEC>(pr + lane * E, po[k]);
       } else {
         pm[k] = kNegInf;
         pl[k] = 0.f;
@@ -1115,8 +1155,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32)
         const int p = p0 + warp + k * kCombineWarps;
         if (p < n_parts) {
           float* pr = clear + row * (D + 4) + p * pstride;
-#pragma unroll
-          for (int e = 0; e < E; ++e) pr[lane * E + e] = 0.f;
+          zero_cols<E, VEC>(pr + lane * E);
           if (lane == 0) *reinterpret_cast<float2*>(pr + D) = make_float2(0.f, 0.f);
         }
       }
@@ -1409,14 +1448,20 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaSuccess;
+  // rows of D+4 floats keep a 16-byte aligned base aligned: vector loads then
+  const bool vec = (reinterpret_cast<uintptr_t>(parts) & 15u) == 0;
+#define QKV_C_LAUNCH(TO, DD, V)                                                             \
+  e = cudaLaunchKernelEx(&cfg, combine_kernel<TO, DD, V>, parts, n_parts, part_stride_rows, \
+                         rows, (TO*)out, op, cl);
 #define QKV_C_CASE(DD)                                                                       \
   case DD:                                                                                   \
-    if (out_dtype == QKV_BF16)                                                               \
-      e = cudaLaunchKernelEx(&cfg, combine_kernel<__nv_bfloat16, DD>, parts, n_parts,        \
-                             part_stride_rows, rows, (__nv_bfloat16*)out, op, cl);           \
-    else                                                                                     \
-      e = cudaLaunchKernelEx(&cfg, combine_kernel<__half, DD>, parts, n_parts,               \
-                             part_stride_rows, rows, (__half*)out, op, cl);                  \
+    if (out_dtype == QKV_BF16) {                                                             \
+      if (vec) { QKV_C_LAUNCH(__nv_bfloat16, DD, true) }                                     \
+      else { QKV_C_LAUNCH(__nv_bfloat16, DD, false) }                                        \
+    } else {                                                                                 \
+      if (vec) { QKV_C_LAUNCH(__half, DD, true) }                                            \
+      else { QKV_C_LAUNCH(__half, DD, false) }                                               \
+    }                                                                                        \
     break;
   switch (D) {
     QKV_C_CASE(64)
@@ -1426,6 +1471,7 @@ int launch_combine(const float* parts, int n_parts, long long part_stride_rows, 
       return QKV_EUNSUPPORTED;
   }
 #undef QKV_C_CASE
+#undef QKV_C_LAUNCH
   return e == cudaSuccess ? QKV_OK : QKV_ECUDA;
 }
 
