@@ -431,25 +431,27 @@ def run_decode(args, name, cfg, rank, world, device):
     full_e2e = torch.tensor([x + 1 for x in full], dtype=torch.int32, device=device)
     n_e2e = max(e2e_loc)
 
+    # per-layer views of the step's device buffers (the copies below refill them every step)
+    views = [(dq[l], dk[l], dv[l], out[l], part_local[l], caches[l].keys, caches[l].values)
+             for l in range(L)]
+
     def e2e_step():
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        for l in range(L):
-            c = caches[l]
+        for ql, kl, vl, ol, pl, kc, vc in views:
             if not sharded and not cfg["ragged"]:
                 # one public call per layer: the kernel appends the token, then attends
-                ops.prefill(dq[l], dk[l], dv[l], c.keys, c.values, pos, bits, scale, out=out[l])
+                ops.prefill(ql, kl, vl, kc, vc, pos, bits, scale, out=ol)
             elif not sharded:
-                ops.quantize_append_kv(dk[l], dv[l], c.keys, c.values, pos, bits)
-                ops.attention(dq[l], c.keys, c.values, scale, pos + 1, bits, lens=lens_e2e,
-                              out=out[l], workspace=ws)
+                ops.quantize_append_kv(kl, vl, kc, vc, pos, bits)
+                ops.attention(ql, kc, vc, scale, pos + 1, bits, lens=lens_e2e, out=ol,
+                              workspace=ws)
             else:
                 if owner:
-                    ops.quantize_append_kv(dk[l], dv[l], c.keys, c.values, pos, bits)
-                ops.attention(dq[l], c.keys, c.values, scale, n_e2e, bits, lens=lens_e2e,
-                              pos_base=base_t, total_lens=full_e2e, out=part_local[l],
-                              out_kind=1, workspace=ws)
+                    ops.quantize_append_kv(kl, vl, kc, vc, pos, bits)
+                ops.attention(ql, kc, vc, scale, n_e2e, bits, lens=lens_e2e, pos_base=base_t,
+                              total_lens=full_e2e, out=pl, out_kind=1, workspace=ws)
         if sharded:
             hout.copy_(dec.merge(part_local, out).view_as(hout), non_blocking=True)
         else:
@@ -465,7 +467,7 @@ def run_decode(args, name, cfg, rank, world, device):
 
     if dec is not None:
         dec.close()
-    del caches, graph
+    del caches, graph, views
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     if rank != 0:

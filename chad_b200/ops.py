@@ -242,10 +242,12 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
     kw, ks, kb = k_quant
     vw, vs, vb = v_quant
     dev = _need_cuda(q, kw, ks, kb, vw, vs, vb, lens, pos_base, total_lens)
-    for t, nm in ((q, "q"), (kw, "kw"), (ks, "ks"), (kb, "kb"), (vw, "vw"), (vs, "vs"), (vb, "vb")):
-        _contig(t, nm)
+    if not (q.is_contiguous() and kw.is_contiguous() and ks.is_contiguous()
+            and kb.is_contiguous() and vw.is_contiguous() and vs.is_contiguous()
+            and vb.is_contiguous()):
+        raise ValueError("q and the quantized cache tensors must be contiguous")
     B, HQ, S, D = q.shape
-    HKV, NP = kw.shape[1], kw.shape[2]
+    _, HKV, NP = kw.shape[:3]
     if out is None:
         if out_kind == _lib.QKV_OUT_NORMALIZED:
             out = torch.empty_like(q)
@@ -255,18 +257,22 @@ def attention(q: torch.Tensor, k_quant: Sequence[torch.Tensor], v_quant: Sequenc
     for t in (lens, pos_base, total_lens):
         if t is not None and t.dtype != torch.int32:
             raise TypeError("lens/pos_base/total_lens must be int32")
-    need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size, dev.index)
-    if splits:
-        # forced split count: rows of at most D + 16 floats per split (D + 2*D/32 merged)
-        need = max(need, splits * B * HQ * S * (D + 16) * 4 + (1 << 16))
-    ws = workspace if workspace is not None else _workspace(dev, need)
-    with _on(dev):
-        check(_lib.fn("qkv_attention")(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
-                                vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(),
-                                B, HQ, HKV, S, D, NP, n, _ptr(lens), _ptr(pos_base),
-                                _ptr(total_lens), bits, group_size, dtype_code(q), float(scale),
-                                kind, _ptr(m), mnk, sb, sh, sq, out_kind, splits,
-                                ws.data_ptr(), ws.numel(), _stream(dev)))
+    idx = dev.index
+    if workspace is None:
+        need = workspace_size(B, HQ, HKV, S, D, max(n, 1), bits, group_size, idx)
+        if splits:
+            # forced split count: rows of at most D + 16 floats per split (D + 2*D/32 merged)
+            need = max(need, splits * B * HQ * S * (D + 16) * 4 + (1 << 16))
+        workspace = _workspace(dev, need)
+    fn = _lib.fn("qkv_attention")
+    switch = idx != torch.cuda.current_device()
+    with (torch.cuda.device(dev) if switch else contextlib.nullcontext()):
+        check(fn(q.data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(), vw.data_ptr(),
+                 vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B, HQ, HKV, S, D, NP, n,
+                 _ptr(lens), _ptr(pos_base), _ptr(total_lens), bits, group_size, dtype_code(q),
+                 float(scale), kind, _ptr(m), mnk, sb, sh, sq, out_kind, splits,
+                 workspace.data_ptr(), workspace.numel(),
+                 _RAW_STREAM(idx) if _RAW_STREAM is not None else _stream(dev)))
         if CHECK_EACH_CALL:
             check_device()
     return out
@@ -326,22 +332,28 @@ def prefill(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
             out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Quantize-append the new chunk at [offset, offset+S) then attend causally over all keys
     (one library call; S = 1 is a decode step)."""
+    # one call per layer per decode step: the host work here is kept to plain attribute reads
     kw, ks, kb = k_quant
     vw, vs, vb = v_quant
     dev = _need_cuda(q, k_new, v_new, kw)
+    if not (q.is_contiguous() and k_new.is_contiguous() and v_new.is_contiguous()):
+        raise ValueError("q, k_new and v_new must be contiguous")
     B, HQ, S, D = q.shape
-    HKV, NP = kw.shape[1], kw.shape[2]
+    _, HKV, NP = kw.shape[:3]
     if out is None:
         out = torch.empty_like(q)
-    need = workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size, dev.index)
-    ws = _workspace(dev, need)
-    with _on(dev):
-        check(_lib.fn("qkv_prefill")(
-            _contig(q, "q").data_ptr(), _contig(k_new, "k_new").data_ptr(),
-            _contig(v_new, "v_new").data_ptr(), kw.data_ptr(), ks.data_ptr(), kb.data_ptr(),
-            vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B, HQ, HKV, S, D, NP,
-            offset, bits, group_size, dtype_code(q), float(scale), ws.data_ptr(), ws.numel(),
-            _stream(dev)))
+    idx = dev.index
+    dt = _DT.get(q.dtype)
+    if dt is None:
+        raise TypeError(f"unsupported dtype {q.dtype}")
+    ws = _workspace(dev, workspace_size(B, HQ, HKV, S, D, offset + S, bits, group_size, idx))
+    fn = _lib.fn("qkv_prefill")
+    switch = idx != torch.cuda.current_device()
+    with (torch.cuda.device(dev) if switch else contextlib.nullcontext()):
+        check(fn(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), kw.data_ptr(), ks.data_ptr(),
+                 kb.data_ptr(), vw.data_ptr(), vs.data_ptr(), vb.data_ptr(), out.data_ptr(), B,
+                 HQ, HKV, S, D, NP, offset, bits, group_size, dt, float(scale), ws.data_ptr(),
+                 ws.numel(), _RAW_STREAM(idx) if _RAW_STREAM is not None else _stream(dev)))
         if CHECK_EACH_CALL:
             check_device()
     return out
