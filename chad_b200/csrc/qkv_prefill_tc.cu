@@ -47,7 +47,12 @@ constexpr int kKT = 128;         // keys per tile (MMA N of Q K^T)
 constexpr int kWarpsTc = 13;
 constexpr int kThreadsTc = kWarpsTc * 32;
 constexpr float kRescaleLog2 = 12.0f;  // P <= 2^12: exact range in bf16 and f16
-constexpr int kPolyPairs = 4;  // > 0: one value pair in kPolyPairs takes exp2_poly2, not the MUFU
+// One value pair in kPolyPairs takes exp2_poly2 (FMA pipe) instead of the MUFU: 1 in 8 for
+// prefill tiles, 1 in 4 for a verify block's key-split tiles (measured: prefill over a 30K
+// prefix 1215 us per layer at 1 in 8, 1235 at 1 in 4, 1233 with none; the 8-token verify
+// 16.25 us at 1 in 4, 16.50 at 1 in 8).
+template <bool SK>
+constexpr int kPolyPairs = SK ? 4 : 8;
 constexpr int kHalf = kKT * 128;       // bytes of one 64-dim half of a K or V tile
 constexpr int kTileBytes = 2 * kHalf;  // one dequantized K or V tile
 #define kNegInfTc (-__int_as_float(0x7f800000))
@@ -530,7 +535,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           for (int e = 0; e < 16; ++e) {
             float u0, u1, p0, p1;
             fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
-            if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
+            if (kPolyPairs<SK> > 0 && e % kPolyPairs<SK> == kPolyPairs<SK> - 1) {
               exp2_poly2(p0, p1, u0, u1);
             } else {
               p0 = ex2(u0);
@@ -580,7 +585,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           m_run = m_cand;
         }
         const float mu = m_run == kNegInfTc ? 0.f : m_run;
-        // pass 2: p = 2^(s*c - mu) (MUFU; one pair in kPolyPairs by the FMA-pipe polynomial),
+        // pass 2: p = 2^(s*c - mu) (MUFU; one pair in kPolyPairs<SK> by the FMA-pipe polynomial),
         // P over S.
         // P chunk ch lands in columns [16ch, 16ch+16), all read already by chunks <= ch.
 #pragma unroll 1
@@ -597,7 +602,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
           for (int e = 0; e < 16; ++e) {
             float u0, u1, p0, p1;
             fma2(u0, u1, __uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]), c, c, -mu, -mu);
-            if (kPolyPairs > 0 && e % kPolyPairs == kPolyPairs - 1) {
+            if (kPolyPairs<SK> > 0 && e % kPolyPairs<SK> == kPolyPairs<SK> - 1) {
               exp2_poly2(p0, p1, u0, u1);
             } else {
               p0 = ex2(u0);
