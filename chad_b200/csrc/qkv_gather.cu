@@ -25,6 +25,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "../../include/qkv.h"
 #include "qkv_common.cuh"
@@ -178,21 +179,24 @@ __global__ void __launch_bounds__(kGatherThreads)
   }
 }
 
-// Resident CTAs of one instantiation on the current device (cached per device).
+// Resident CTAs of one instantiation on the current device (cached per device; threads
+// that race here compute the same value).
 template <typename TO, int D>
 int gather_grid_cap() {
-  static int cap[kMaxDevices] = {};
+  static std::atomic<int> cap[kMaxDevices];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
-  if (cap[dev] == 0) {
+  int c = cap[dev].load(std::memory_order_relaxed);
+  if (c == 0) {
     int per_sm = 0, sms = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gather_combine_kernel<TO, D>,
                                                       kGatherThreads, 0) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return 0;
-    cap[dev] = per_sm * sms;
+    c = per_sm * sms;
+    cap[dev].store(c, std::memory_order_relaxed);
   }
-  return cap[dev];
+  return c;
 }
 
 }  // namespace
