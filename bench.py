@@ -19,8 +19,9 @@ With N GPUs (torchrun, one process per GPU) the sequences are sharded along the 
 (chad_b200.shard): every rank holds a contiguous range of each sequence, writes one (max,
 sum, out) partial row per query row per layer, and ShardedDecoder merges the rows with one
 qkv_gather_combine launch per rank (each rank writes its rows into every rank's buffer over
-NVLink peer memory, waits for the others' and merges). The NCCL transport (one all_gather,
-then the combine kernel) is timed beside it. The headline keeps 32K keys per GPU (weak
+NVLink peer memory, waits for the others' and merges) up to 4 GPUs, and with one NCCL
+all_gather and the combine kernel at 8, where that is faster for one large merge
+(ShardedDecoder "auto"); both transports are also timed on their own beside it. The headline keeps 32K keys per GPU (weak
 scaling, context 32K*N); the nested long-context line keeps the total work fixed (strong
 scaling, the same B4 64K-128K sequences split N ways), timed both with one merge per step
 (layers independent) and with a merge after every layer (a model that serialises its
@@ -302,9 +303,14 @@ def run_decode(args, name, cfg, rank, world, device):
     keys_rank = sum(loc)  # this rank's keys per layer (all batch rows)
     kv_bytes_rank = keys_rank * HKV * kv_bytes_per_key(D, bits)
     # the step's merge: one qkv_gather_combine launch per rank (rows over NVLink peer
-    # memory); the NCCL all_gather + combine transport is timed beside it
-    dec = ShardedDecoder(transport="peer") if sharded else None
+    # memory) up to 4 GPUs, one all_gather + combine at 8 ("auto", see chad_b200.shard);
+    # both transports are also timed on their own beside it
+    dec = ShardedDecoder(transport="auto") if sharded else None
+    dec_peer = ShardedDecoder(transport="peer") if sharded else None
     dec_nccl = ShardedDecoder() if sharded else None
+    step_rows = L * B * HQ
+    step_peer = sharded and dec.uses_peer(step_rows)
+    step_dst = out if step_peer else gathered  # the merged output, or NCCL's gather buffer
 
     def attn(l, qq, n, lens, parts_out=None):
         c = caches[l]
@@ -324,7 +330,7 @@ def run_decode(args, name, cfg, rank, world, device):
     def step():
         graph.replay()
         if sharded:
-            dec.merge(part_local, out)
+            dec.merge(part_local, step_dst)
 
     ms, clocks = _timed(step, args.steps, args.warmup, world, device)
 
@@ -350,7 +356,7 @@ def run_decode(args, name, cfg, rank, world, device):
     # per-layer gather (N > 1): attention -> all_gather -> combine after every layer, the
     # dependency chain of a model that serialises its layers; all 48 layers captured in one
     # CUDA graph with the collectives (eager launches if capture is refused)
-    per_layer = step_nccl_res = None
+    per_layer = step_nccl_res = step_peer_res = None
     if sharded:
         gl = torch.empty((world, 1, B, HQ, 1, D + 4), dtype=torch.float32, device=device)
 
@@ -388,7 +394,7 @@ def run_decode(args, name, cfg, rank, world, device):
         def per_layer_peer_calls():
             for l in range(L):
                 attn(l, q[l], nloc, lens_t, part_local[l])
-                dec.merge(part_local[l:l + 1], out[l:l + 1])
+                dec_peer.merge(part_local[l:l + 1], out[l:l + 1])
 
         gpp = _graph(per_layer_peer_calls, stream)
         ms_pp, _ = _timed(gpp.replay, max(3, min(50, args.steps)), 2, world, device, clocks=False)
@@ -412,6 +418,19 @@ def run_decode(args, name, cfg, rank, world, device):
                                         / (ms_sn * 1e-3) / 1e9, 2),
                          "how": "the step's graph, then one NCCL all_gather_into_tensor and "
                                 "the combine kernel; max over ranks"}
+
+        # the step with the peer transport: one qkv_gather_combine launch for all layers
+        def step_peer_only():
+            graph.replay()
+            dec_peer.merge(part_local, out)
+
+        ms_sp, _ = _timed(step_peer_only, max(3, min(50, args.steps)), 2, world, device,
+                          clocks=False)
+        step_peer_res = {"ms_per_step": round(ms_sp, 5), "us_per_layer": round(ms_sp * 1e3 / L, 3),
+                         "value": round(_sum_over_ranks(kv_bytes_rank, world, device) * L
+                                        / (ms_sp * 1e-3) / 1e9, 2),
+                         "how": "the step's graph, then one qkv_gather_combine launch; max over "
+                                "ranks"}
         del gpp
         torch.cuda.synchronize()
 
@@ -453,7 +472,7 @@ def run_decode(args, name, cfg, rank, world, device):
                 ops.attention(ql, kc, vc, scale, n_e2e, bits, lens=lens_e2e, pos_base=base_t,
                               total_lens=full_e2e, out=pl, out_kind=1, workspace=ws)
         if sharded:
-            hout.copy_(dec.merge(part_local, out).view_as(hout), non_blocking=True)
+            hout.copy_(dec.merge(part_local, step_dst).view_as(hout), non_blocking=True)
         else:
             hout.copy_(out, non_blocking=True)
 
@@ -467,6 +486,7 @@ def run_decode(args, name, cfg, rank, world, device):
 
     if dec is not None:
         dec.close()
+        dec_peer.close()
     del caches, graph, views
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -499,8 +519,9 @@ def run_decode(args, name, cfg, rank, world, device):
             "kv_bits": bits, "group_size": 64, "layers_per_step": L,
             "l2": f"inputs larger than L2: {L} distinct layer caches, "
                   f"{kv_bytes_rank * L / 1e9:.2f} GB per GPU",
-            "parallelism": (f"sequence-sharded split-KV x{world}, one qkv_gather_combine "
-                            "per step (partial rows over NVLink peer memory)"
+            "parallelism": ((f"sequence-sharded split-KV x{world}, one merge per step: "
+                             + ("qkv_gather_combine (partial rows over NVLink peer memory)"
+                                if step_peer else "NCCL all_gather + combine kernel"))
                             if sharded else "single GPU"),
         },
         "roofline": {
@@ -525,6 +546,7 @@ def run_decode(args, name, cfg, rank, world, device):
     if per_layer is not None:
         res["per_layer_gather"] = per_layer
         res["step_merge_nccl"] = step_nccl_res
+        res["step_merge_peer"] = step_peer_res
     return res
 
 
