@@ -19,9 +19,8 @@ With N GPUs (torchrun, one process per GPU) the sequences are sharded along the 
 (chad_b200.shard): every rank holds a contiguous range of each sequence, writes one (max,
 sum, out) partial row per query row per layer, and ShardedDecoder merges the rows with one
 qkv_gather_combine launch per rank (each rank writes its rows into every rank's buffer over
-NVLink peer memory, waits for the others' and merges) up to 4 GPUs, and with one NCCL
-all_gather and the combine kernel at 8, where that is faster for one large merge
-(ShardedDecoder "auto"); both transports are also timed on their own beside it. The headline keeps 32K keys per GPU (weak
+NVLink peer memory, waits for the others' and merges); the NCCL transport (one all_gather,
+then the combine kernel) and the peer kernel are also timed on their own beside it. The headline keeps 32K keys per GPU (weak
 scaling, context 32K*N); the nested long-context line keeps the total work fixed (strong
 scaling, the same B4 64K-128K sequences split N ways), timed both with one merge per step
 (layers independent) and with a merge after every layer (a model that serialises its
@@ -122,8 +121,9 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, index):
+    def __init__(self, index, period=0.01):
         self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period
         self._stop = threading.Event()
         try:
             import pynvml
@@ -145,7 +145,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:  # noqa: BLE001
                 pass
-            time.sleep(0.01)
+            time.sleep(self.period)
 
     def __enter__(self):
         if self.nv:
@@ -244,7 +244,12 @@ def _timed(fn, steps, warmup, world, device, clocks=True):
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(torch.cuda.current_device()) if clocks else None
+    # Clocks are sampled by rank 0 alone, every 10 ms on one GPU and every 50 ms with more:
+    # NVML polling from every rank at 100 Hz was measured to slow the 8-GPU step itself
+    # (25.1 against 14.5 us per layer in the same run).
+    rank0 = world == 1 or dist.get_rank() == 0
+    sampler = (ClockSampler(torch.cuda.current_device(), 0.01 if world == 1 else 0.05)
+               if clocks and rank0 else None)
     if sampler:
         sampler.__enter__()
     ev0.record()
@@ -303,14 +308,10 @@ def run_decode(args, name, cfg, rank, world, device):
     keys_rank = sum(loc)  # this rank's keys per layer (all batch rows)
     kv_bytes_rank = keys_rank * HKV * kv_bytes_per_key(D, bits)
     # the step's merge: one qkv_gather_combine launch per rank (rows over NVLink peer
-    # memory) up to 4 GPUs, one all_gather + combine at 8 ("auto", see chad_b200.shard);
-    # both transports are also timed on their own beside it
-    dec = ShardedDecoder(transport="auto") if sharded else None
+    # memory); both transports are also timed on their own beside it
+    dec = ShardedDecoder(transport="peer") if sharded else None
     dec_peer = ShardedDecoder(transport="peer") if sharded else None
     dec_nccl = ShardedDecoder() if sharded else None
-    step_rows = L * B * HQ
-    step_peer = sharded and dec.uses_peer(step_rows)
-    step_dst = out if step_peer else gathered  # the merged output, or NCCL's gather buffer
 
     def attn(l, qq, n, lens, parts_out=None):
         c = caches[l]
@@ -330,7 +331,7 @@ def run_decode(args, name, cfg, rank, world, device):
     def step():
         graph.replay()
         if sharded:
-            dec.merge(part_local, step_dst)
+            dec.merge(part_local, out)
 
     ms, clocks = _timed(step, args.steps, args.warmup, world, device)
 
@@ -472,7 +473,7 @@ def run_decode(args, name, cfg, rank, world, device):
                 ops.attention(ql, kc, vc, scale, n_e2e, bits, lens=lens_e2e, pos_base=base_t,
                               total_lens=full_e2e, out=pl, out_kind=1, workspace=ws)
         if sharded:
-            hout.copy_(dec.merge(part_local, step_dst).view_as(hout), non_blocking=True)
+            hout.copy_(dec.merge(part_local, out).view_as(hout), non_blocking=True)
         else:
             hout.copy_(out, non_blocking=True)
 
@@ -519,9 +520,8 @@ def run_decode(args, name, cfg, rank, world, device):
             "kv_bits": bits, "group_size": 64, "layers_per_step": L,
             "l2": f"inputs larger than L2: {L} distinct layer caches, "
                   f"{kv_bytes_rank * L / 1e9:.2f} GB per GPU",
-            "parallelism": ((f"sequence-sharded split-KV x{world}, one merge per step: "
-                             + ("qkv_gather_combine (partial rows over NVLink peer memory)"
-                                if step_peer else "NCCL all_gather + combine kernel"))
+            "parallelism": (f"sequence-sharded split-KV x{world}, one qkv_gather_combine "
+                            "per step (partial rows over NVLink peer memory)"
                             if sharded else "single GPU"),
         },
         "roofline": {

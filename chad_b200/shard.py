@@ -12,11 +12,6 @@ across GPUs instead of across blocks. Two transports move the rows:
           every rank's receive buffer over NVLink (buffers mapped into every process with
           CUDA IPC), waits for the other ranks' rows and merges them. No collective, no
           second launch, and it captures in a CUDA graph.
-  "auto"  "peer" for merges of at most PEER_MAX_ROWS rows or on at most PEER_MAX_WORLD
-          ranks, "nccl" otherwise. Measured (48-layer decode steps): the peer kernel wins
-          every per-layer merge (22.4 vs 35.8 us per layer at 8 GPUs) and the one-per-step
-          merge up to 4 GPUs, but at 8 GPUs a merge of 1536 rows or more, where its
-          flag-per-word stores double the bytes, loses to NCCL (20.2 vs 14.7 us per layer).
 
 Several layers can share the one exchange when their inputs are independent (`layers` axis).
 
@@ -40,10 +35,6 @@ def shard_ranges(lens: Sequence[int], world: int, rank: int) -> Tuple[List[int],
         base.append(lo)
         loc.append(hi - lo)
     return base, loc
-
-
-PEER_MAX_ROWS = 256   # "auto": merges this small always take the peer kernel
-PEER_MAX_WORLD = 4    # "auto": up to this many ranks every merge takes the peer kernel
 
 
 class PeerGather:
@@ -145,8 +136,8 @@ class ShardedDecoder:
                  combine_fn: Optional[Callable] = None, transport: str = "nccl"):
         import torch.distributed as dist
 
-        if transport not in ("nccl", "peer", "auto"):
-            raise ValueError(f"transport must be 'nccl', 'peer' or 'auto', not {transport!r}")
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport must be 'nccl' or 'peer', not {transport!r}")
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -182,9 +173,8 @@ class ShardedDecoder:
     def merge(self, local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Gather this rank's partial rows (any leading layer axes) with every other rank's
         and merge them: the cross-GPU pass 2. Several layers may share the one gather.
-        `out` is the gather buffer for the "nccl" transport, the merged output for "peer"
-        (so with "auto", pass None or the buffer matching the transport `uses_peer` picks)."""
-        if self.world > 1 and self.uses_peer(local.numel() // local.shape[-1]):
+        `out` is the gather buffer for the "nccl" transport, the merged output for "peer"."""
+        if self.world > 1 and self.transport == "peer":
             D = local.shape[-1] - 4
             key = (local.numel() // (D + 4), D)
             pg = self._peer.get(key)
@@ -192,12 +182,6 @@ class ShardedDecoder:
                 pg = self._peer[key] = PeerGather(key[0], D, self.group, local.device)
             return pg.combine(local, out=out)
         return self.combine_fn(self.gather(local, out))
-
-    def uses_peer(self, rows: int) -> bool:
-        """Whether a merge of `rows` partial rows takes the peer kernel."""
-        if self.transport == "auto":
-            return rows <= PEER_MAX_ROWS or self.world <= PEER_MAX_WORLD
-        return self.transport == "peer"
 
     def close(self) -> None:
         """Release the peer transport's buffers (collective)."""

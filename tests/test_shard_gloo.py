@@ -135,16 +135,3 @@ def test_transport_choice_is_checked():
     assert dec.gather(local).shape == (1, 2, 1, 4, 1, 68)
     dec.close()
 
-
-def test_auto_transport_picks_by_merge_size():
-    from chad_b200 import shard
-    from chad_b200.shard import ShardedDecoder
-
-    dec = ShardedDecoder(transport="auto")
-    dec.world = 8
-    assert dec.uses_peer(32) and dec.uses_peer(shard.PEER_MAX_ROWS)
-    assert not dec.uses_peer(1536) and not dec.uses_peer(6144)
-    dec.world = shard.PEER_MAX_WORLD
-    assert dec.uses_peer(6144)
-    assert ShardedDecoder(transport="peer").uses_peer(10 ** 6)
-    assert not ShardedDecoder(transport="nccl").uses_peer(1)
