@@ -40,7 +40,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -112,7 +111,10 @@ def chunk_flops(cfg):
 
 
 class ClockSampler:
-    """NVML sampling of SM clocks and throttle reasons while the timed region runs."""
+    """SM clocks and throttle reasons sampled by a separate `nvidia-smi -lms` process while
+    the timed region runs. Sampling from a thread of the timed process itself (NVML calls
+    and GIL hand-offs) was measured to stall its launch loop: in an 8-GPU step a few ms
+    at the start of a ~15 ms region, which every other rank then waited for."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -123,45 +125,69 @@ class ClockSampler:
 
     def __init__(self, index, period=0.01):
         self.samples, self.reasons, self.max_mhz = [], set(), None
-        self.period = period
-        self._stop = threading.Event()
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        self.period_ms = max(10, int(round(period * 1000)))
+        self.proc = None
+        self.ids = [str(index)]
+        try:  # the PCI bus id names the same GPU whatever the enumeration order
+            prop = torch.cuda.get_device_properties(index)
+            bus = getattr(prop, "pci_bus_id", None)
+            if bus is not None:
+                dom = getattr(prop, "pci_domain_id", 0)
+                dev = getattr(prop, "pci_device_id", 0)
+                self.ids.insert(0, f"{dom:08X}:{bus:02X}:{dev:02X}.0")
         except Exception:  # noqa: BLE001
-            self.nv = None
+            pass
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit and name != "gpu_idle":
-                        self.reasons.add(name)
-            except Exception:  # noqa: BLE001
-                pass
-            time.sleep(self.period)
+    def _parse(self, line):
+        parts = [x.strip() for x in line.split(",")]
+        if len(parts) < 3:
+            return
+        try:
+            self.samples.append(float(parts[0]))
+            self.max_mhz = int(float(parts[1]))
+            r = int(parts[2], 16)
+        except ValueError:
+            return
+        for bit, name in self.REASONS.items():
+            if r & bit and name != "gpu_idle":
+                self.reasons.add(name)
 
     def __enter__(self):
-        if self.nv:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
+        import subprocess
+
+        for gpu in self.ids:
+            cmd = ["nvidia-smi", f"--id={gpu}",
+                   "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                   "--format=csv,noheader,nounits", f"-lms={self.period_ms}"]
+            try:
+                proc = subprocess.Popen(cmd, stdout=subprocess.PIPE,
+                                        stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                return self
+            first = proc.stdout.readline()  # sampling runs before the region starts
+            if first:
+                self.proc = proc
+                self._parse(first)
+                return self
+            proc.wait()
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        if self.nv:
-            self._t.join()
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            rest, _ = self.proc.communicate(timeout=10)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+            rest, _ = self.proc.communicate()
+        for line in (rest or "").splitlines():
+            self._parse(line)
 
     def summary(self):
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                "samples": len(self.samples)}
+                "samples": len(self.samples), "sampler": "nvidia-smi -lms %d" % self.period_ms}
 
 
 # ---------------------------------------------------------------------------------------
@@ -244,9 +270,8 @@ def _timed(fn, steps, warmup, world, device, clocks=True):
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # Clocks are sampled by rank 0 alone, every 10 ms on one GPU and every 50 ms with more:
-    # NVML polling from every rank at 100 Hz was measured to slow the 8-GPU step itself
-    # (25.1 against 14.5 us per layer in the same run).
+    # Clocks are sampled by rank 0 alone (every 10 ms on one GPU, every 50 ms with more),
+    # from a separate process: see ClockSampler.
     rank0 = world == 1 or dist.get_rank() == 0
     sampler = (ClockSampler(torch.cuda.current_device(), 0.01 if world == 1 else 0.05)
                if clocks and rank0 else None)
