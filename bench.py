@@ -266,17 +266,18 @@ def _timed(fn, steps, warmup, world, device, clocks=True):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # Clocks are sampled by rank 0 alone (every 10 ms on one GPU, every 50 ms with more),
-    # from a separate process: see ClockSampler.
+    # from a separate process (see ClockSampler), started before the barrier: a rank that
+    # starts late would hold every other rank's merge inside their timed regions.
     rank0 = world == 1 or dist.get_rank() == 0
     sampler = (ClockSampler(torch.cuda.current_device(), 0.01 if world == 1 else 0.05)
                if clocks and rank0 else None)
     if sampler:
         sampler.__enter__()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(steps):
         fn()
