@@ -124,3 +124,17 @@ def test_shard_ranges_cover_every_key():
                 got.extend(range(lo, lo + n))
             assert got == list(range(L))
     assert np.all(np.array(shard_ranges([10], 4, 3)[1]) >= 0)
+
+
+def test_bench_clock_sampler_parses_nvidia_smi_lines():
+    """bench.py's clock record: SM MHz median, max clock and the throttle reasons named
+    from the bit mask (gpu_idle dropped); malformed lines are skipped."""
+    import bench
+
+    c = bench.ClockSampler(0, 0.05)
+    for line in ("1965, 1965, 0x0000000000000000", "1950, 1965, 0x0000000000000004",
+                 "1900, 1965, 0x0000000000000001", "not a sample", "1965, 1965, 0x48"):
+        c._parse(line)
+    sm = c.summary()
+    assert sm["samples"] == 4 and sm["sm_max_mhz"] == 1965 and sm["sm_mhz"] == 1957.5
+    assert sm["reasons"] == ["hw_slowdown", "hw_thermal_slowdown", "sw_power_cap"]
