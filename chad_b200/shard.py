@@ -41,7 +41,8 @@ class PeerGather:
     """Receive buffers of qkv_gather_combine for one row shape, one per rank, each mapped
     into every rank's process. Built collectively (every rank, same order); `close` too."""
 
-    def __init__(self, rows: int, D: int, group=None, device=None):
+    def __init__(self, rows: int, D: int, group=None, device=None, lib=None):
+        """`lib`: the library to call (the loaded libqkv.so; a stand-in in host tests)."""
         import ctypes
 
         import torch.distributed as dist
@@ -54,13 +55,13 @@ class PeerGather:
         self.rows, self.D = int(rows), int(D)
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
-        lib = _lib.load()
+        self.lib = lib = lib if lib is not None else _lib.load()
         self.nbytes = lib.qkv_gather_buffer_size(self.rows, self.D, self.world)
         if self.nbytes == 0:
             raise ValueError(f"qkv_gather_buffer_size: unsupported shape rows={rows} D={D}")
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(_lib.QKV_IPC_HANDLE_BYTES)
-        with torch.cuda.device(self.device):
+        with self._on_device():
             _lib.check(lib.qkv_peer_alloc(self.nbytes, ctypes.byref(own), handle))
         self._own = own.value
         handles: List[Optional[bytes]] = [None] * self.world
@@ -68,7 +69,7 @@ class PeerGather:
         self._opened: List[int] = []
         ptrs = []
         try:
-            with torch.cuda.device(self.device):
+            with self._on_device():
                 for p, h in enumerate(handles):
                     if p == self.rank:
                         ptrs.append(self._own)
@@ -105,12 +106,17 @@ class PeerGather:
                 ops._stream(local.device)))
         return out
 
-    def _release(self, barrier: bool) -> None:
-        from . import _lib
+    def _on_device(self):
+        import contextlib
 
-        lib = _lib.load()
-        with torch.cuda.device(self.device):
-            torch.cuda.synchronize()
+        return torch.cuda.device(self.device) if self.device.type == "cuda" \
+            else contextlib.nullcontext()
+
+    def _release(self, barrier: bool) -> None:
+        lib = self.lib
+        with self._on_device():
+            if self.device.type == "cuda":
+                torch.cuda.synchronize()
             for p in self._opened:
                 lib.qkv_peer_free(p, 1)
             self._opened = []

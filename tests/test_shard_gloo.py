@@ -135,3 +135,72 @@ def test_transport_choice_is_checked():
     assert dec.gather(local).shape == (1, 2, 1, 4, 1, 68)
     dec.close()
 
+
+
+class _FakePeerLib:
+    """Stand-in for libqkv's peer-buffer entry points: buffer pointers and IPC handles are
+    made up per rank, opened mappings recorded, frees logged in order."""
+
+    def __init__(self, rank):
+        self.rank, self.log = rank, []
+
+    def qkv_gather_buffer_size(self, rows, D, world):
+        return rows * (D + 4) * world * 16 + rows * 4
+
+    def qkv_peer_alloc(self, nbytes, own_ref, handle):
+        import ctypes
+
+        own_ref._obj.value = 0x100000 * (self.rank + 1)
+        tag = b"rank%d" % self.rank
+        ctypes.memmove(handle, tag, len(tag))
+        self.log.append(("alloc", nbytes))
+        return 0
+
+    def qkv_peer_open(self, h, mapped_ref):
+        r = int(bytes(h).split(b"\0")[0][4:])
+        mapped_ref._obj.value = 0x7000000 + 0x100000 * (r + 1)
+        self.log.append(("open", r))
+        return 0
+
+    def qkv_peer_free(self, ptr, opened):
+        self.log.append(("free", ptr, opened))
+        return 0
+
+
+def _peer_setup_worker(rank, world, port, q):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from chad_b200.shard import PeerGather
+
+        lib = _FakePeerLib(rank)
+        pg = PeerGather(4, 128, device="cpu", lib=lib)
+        ptrs = pg.peer_ptrs.tolist()
+        pg.close()
+        pg.close()  # a second close is a no-op
+        q.put((rank, ptrs, lib.log))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_transport_setup_exchanges_handles_and_frees_in_order():
+    """The host side of the peer transport on two gloo ranks: every rank's pointer table
+    holds its own buffer at its rank and the other rank's buffer as opened from that rank's
+    handle; teardown closes the mappings before the own buffer is freed."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_setup_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = sorted(q.get(timeout=5) for _ in range(world))
+    for rank, ptrs, log in got:
+        other = 1 - rank
+        assert ptrs[rank] == 0x100000 * (rank + 1)
+        assert ptrs[other] == 0x7000000 + 0x100000 * (other + 1)
+        assert ("open", other) in log and ("open", rank) not in log
+        frees = [e for e in log if e[0] == "free"]
+        assert frees == [("free", ptrs[other], 1), ("free", ptrs[rank], 0)]
